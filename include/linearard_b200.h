@@ -1,0 +1,146 @@
+/*
+ * linearard_b200.h -- C ABI of the B200 (sm_100a) attention-relation KL loss.
+ *
+ * The loss, for every (batch b, query head h, row i):
+ *   KL_i = sum_j pt_ij * (log pt_ij - log ps_ij),
+ *   ps_ij = softmax_j(sc_s * qs_i . ks_j),  pt_ij = softmax_j(sc_t * qt_i . kt_j),
+ * over the columns j that are valid for row i (padding mask on row and column,
+ * and j <= i when causal).  The kv head of query head h is h / (Hq / Hkv).
+ * Every function returns the sum over rows, never an n x n map.
+ *
+ * Each entry point replaces one operator of LinearARD's
+ * kernels/attention_KL package (paths are inside that project):
+ *   lkl_lse          <- lse_stats_triton    kernels/attention_KL/kernel_A.py:190-265
+ *   lkl_kl_forward   <- kl_forward_triton   kernels/attention_KL/kernel_B.py:249-391
+ *   lkl_forward      <- AttnKLAlignFn.forward (A, A, B chained)
+ *                                           kernels/attention_KL/integration.py:8-45
+ *   lkl_backward     <- kl_backward_triton + the dloss chain rule of
+ *                       AttnKLAlignFn.backward
+ *                                           kernels/attention_KL/kernel_C.py:293-449,
+ *                                           kernels/attention_KL/integration.py:48-67
+ *
+ * Conventions
+ *  - Plain device pointers.  q/k tensors are contiguous [B, H, T, D] fp16 or
+ *    bf16 (last stride 1), lse tensors contiguous fp32 [B, Hq, T].
+ *  - mask: NULL (no padding) or a device pointer to a contiguous [B, T] array
+ *    of LKL_MASK_* elements, nonzero = valid token.
+ *  - All work is enqueued on `stream`; nothing synchronises the host.
+ *  - Scratch memory is caller-provided (`workspace`, `workspace_bytes`); query
+ *    the size with lkl_workspace_size().  The library never allocates.
+ *  - Return value: LKL_OK or an LKL_ERR_* code; lkl_status_string() names it.
+ *    Validation mirrors the reference wrappers' assertions.
+ */
+#ifndef LINEARARD_B200_H_
+#define LINEARARD_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LKL_ABI_VERSION 1
+
+/* element types of q/k tensors */
+enum lkl_dtype { LKL_F16 = 0, LKL_BF16 = 1 };
+
+/* element types accepted for the [B, T] padding mask (kernel_A.py:215-217) */
+enum lkl_mask_dtype { LKL_MASK_BOOL = 0, LKL_MASK_U8 = 1, LKL_MASK_I32 = 2, LKL_MASK_I64 = 3 };
+
+/* status codes */
+enum lkl_status {
+  LKL_OK = 0,
+  LKL_ERR_NULL_POINTER = 1,     /* a required pointer is NULL                        */
+  LKL_ERR_BAD_SHAPE = 2,        /* B/T/H mismatch, Hq % Hkv != 0, non-positive sizes */
+  LKL_ERR_BAD_HEAD_DIM = 3,     /* D not in {8,16,32,64,128,256}                     */
+  LKL_ERR_BAD_DTYPE = 4,        /* unknown lkl_dtype / lkl_mask_dtype                */
+  LKL_ERR_MISALIGNED = 5,       /* pointer not aligned to its element size           */
+  LKL_ERR_WORKSPACE = 6,        /* workspace NULL or smaller than lkl_workspace_size */
+  LKL_ERR_LAUNCH = 7,           /* a kernel launch or driver call failed             */
+  LKL_ERR_NO_DEVICE = 8,        /* current device is not sm_100 / no CUDA device     */
+  LKL_ERR_DEVICE_TIMEOUT = 9,   /* a device-side bounded wait expired (see below)    */
+  LKL_ERR_BAD_ALIAS = 10,       /* dq == dk requires qs == ks and Hkv_s == Hq        */
+  LKL_ERR_TOO_LARGE = 11        /* a size exceeds what the entry point supports      */
+};
+
+/* Shape / option block shared by every entry point. */
+typedef struct lkl_problem {
+  int32_t B;          /* batch                                               */
+  int32_t Hq;         /* query heads (student and teacher)                   */
+  int32_t Hkv_s;      /* student key heads, Hq % Hkv_s == 0                   */
+  int32_t Hkv_t;      /* teacher key heads, Hq % Hkv_t == 0                   */
+  int32_t T;          /* sequence length                                     */
+  int32_t Ds;         /* student head dim                                    */
+  int32_t Dt;         /* teacher head dim                                    */
+  int32_t dtype_s;    /* lkl_dtype of qs/ks                                  */
+  int32_t dtype_t;    /* lkl_dtype of qt/kt                                  */
+  int32_t causal;     /* nonzero: keep j <= i                                */
+  int32_t mask_dtype; /* lkl_mask_dtype, ignored when mask == NULL           */
+  float sm_scale_s;   /* <= 0 selects 1/sqrt(Ds)                              */
+  float sm_scale_t;   /* <= 0 selects 1/sqrt(Dt)                              */
+} lkl_problem;
+
+/* ABI version (LKL_ABI_VERSION) and a static status description. */
+int32_t lkl_abi_version(void);
+const char* lkl_status_string(int32_t status);
+
+/* Bytes of scratch the entry points need for problem `p` (has_mask != 0 when a
+ * padding mask will be passed).  Always a multiple of 256. */
+size_t lkl_workspace_size(const lkl_problem* p, int32_t has_mask);
+
+/* Row log-sum-exp of one (q, k) pair -> lse [B, Hq, T] fp32.
+ * Uses (Hkv_s, Ds, dtype_s, sm_scale_s) of `p`; rows removed by the mask get 0,
+ * rows with no valid column get -inf (kernel_A.py:146-158).
+ * Replaces lse_stats_triton, kernels/attention_KL/kernel_A.py:190-265. */
+int32_t lkl_lse(const void* q, const void* k, const void* mask, const lkl_problem* p,
+                float* lse, void* workspace, size_t workspace_bytes, void* stream);
+
+/* KL sum given precomputed row LSEs -> *loss (fp32 device scalar, overwritten).
+ * Replaces kl_forward_triton, kernels/attention_KL/kernel_B.py:249-391. */
+int32_t lkl_kl_forward(const void* qs, const void* ks, const float* lse_s,
+                       const void* qt, const void* kt, const float* lse_t,
+                       const void* mask, const lkl_problem* p, float* loss,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Fused forward: writes lse_s, lse_t [B, Hq, T] and *loss (sum of row KLs)
+ * in one pass over the causal column tiles.  The loss is reduced
+ * deterministically (fixed order).
+ * Replaces AttnKLAlignFn.forward, kernels/attention_KL/integration.py:8-45. */
+int32_t lkl_forward(const void* qs, const void* ks, const void* qt, const void* kt,
+                    const void* mask, const lkl_problem* p,
+                    float* lse_s, float* lse_t, float* loss,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward: dq [B, Hq, T, Ds] and dk [B, Hkv_s, T, Ds], fp32, both multiplied
+ * by *dloss (a device fp32 scalar; NULL means 1).  dq and dk are overwritten.
+ * If dk == dq (allowed only when qs == ks and Hkv_s == Hq, the symmetric call
+ * attn_kl_align(qs, qs, qt, qt) made by train.py:380-402), the buffer receives
+ * dq + dk, the gradient of the shared tensor.
+ * Replaces kl_backward_triton (kernels/attention_KL/kernel_C.py:293-449) and
+ * the chain rule in AttnKLAlignFn.backward (integration.py:48-67). */
+int32_t lkl_backward(const void* qs, const void* ks, const float* lse_s,
+                     const void* qt, const void* kt, const float* lse_t,
+                     const void* mask, const lkl_problem* p, const float* dloss,
+                     float* dq, float* dk, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* Device-side error word of the current device: the bounded waits inside the
+ * tensor-core kernels set it instead of hanging.  Reads (synchronously) and
+ * clears it; returns LKL_OK or LKL_ERR_DEVICE_TIMEOUT. */
+int32_t lkl_device_status(void);
+
+/* Which implementation the last lkl_forward / lkl_backward call on this host
+ * thread dispatched to: 1 = sm_100a tensor-core kernels, 0 = generic CUDA-core
+ * kernels (head dims or alignments the tensor-core kernels do not cover). */
+int32_t lkl_last_path(void);
+
+/* Force the generic CUDA-core kernels (nonzero) or allow the tensor-core path
+ * (0, the default); process-wide.  For parity tests that cross-check paths. */
+void lkl_set_force_generic(int32_t force);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LINEARARD_B200_H_ */

@@ -1,0 +1,283 @@
+// C ABI entry points (include/linearard_b200.h): argument validation that
+// mirrors the assertions of LinearARD's wrappers (kernel_A.py:190-227,
+// kernel_B.py:262-331, kernel_C.py:306-375), scratch layout, and dispatch to
+// the sm_100a tensor-core kernels or the generic CUDA-core kernels.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include <atomic>
+
+#include "lkl_common.cuh"
+
+namespace {
+
+using lkl::Problem;
+
+thread_local int32_t t_last_path = -1;
+std::atomic<int32_t> g_force_generic{0};
+
+inline bool head_dim_ok(int d) {
+  return d == 8 || d == 16 || d == 32 || d == 64 || d == 128 || d == 256;
+}
+
+inline size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
+
+inline size_t bits_bytes(const lkl_problem* p) {
+  return round256((size_t)p->B * (size_t)((p->T + 31) / 32) * sizeof(uint32_t));
+}
+
+inline int max_partials(const Problem& q) {
+  const int a = lkl::generic_num_partials(q), b = lkl::sm100_num_partials(q);
+  return a > b ? a : b;
+}
+
+Problem to_problem(const lkl_problem* p) {
+  Problem q;
+  q.B = p->B;
+  q.Hq = p->Hq;
+  q.Hkv_s = p->Hkv_s;
+  q.Hkv_t = p->Hkv_t;
+  q.T = p->T;
+  q.Ds = p->Ds;
+  q.Dt = p->Dt;
+  q.dtype_s = p->dtype_s;
+  q.dtype_t = p->dtype_t;
+  q.causal = p->causal ? 1 : 0;
+  q.sc_s = p->sm_scale_s > 0.f ? p->sm_scale_s : 1.0f / sqrtf((float)p->Ds);
+  q.sc_t = p->sm_scale_t > 0.f ? p->sm_scale_t : 1.0f / sqrtf((float)p->Dt);
+  return q;
+}
+
+// Shape / dtype checks shared by every entry point.  `teacher` = the teacher
+// pair (Hkv_t, Dt, dtype_t) is also used.
+int32_t check_problem(const lkl_problem* p, bool teacher) {
+  if (!p) return LKL_ERR_NULL_POINTER;
+  if (p->B < 0 || p->T < 0 || p->Hq <= 0 || p->Hkv_s <= 0) return LKL_ERR_BAD_SHAPE;
+  if (p->Hq % p->Hkv_s != 0) return LKL_ERR_BAD_SHAPE;
+  if (!head_dim_ok(p->Ds)) return LKL_ERR_BAD_HEAD_DIM;
+  if (p->dtype_s != LKL_F16 && p->dtype_s != LKL_BF16) return LKL_ERR_BAD_DTYPE;
+  if (teacher) {
+    if (p->Hkv_t <= 0 || p->Hq % p->Hkv_t != 0) return LKL_ERR_BAD_SHAPE;
+    if (!head_dim_ok(p->Dt)) return LKL_ERR_BAD_HEAD_DIM;
+    if (p->dtype_t != LKL_F16 && p->dtype_t != LKL_BF16) return LKL_ERR_BAD_DTYPE;
+  }
+  if (p->mask_dtype < LKL_MASK_BOOL || p->mask_dtype > LKL_MASK_I64) return LKL_ERR_BAD_DTYPE;
+  // grid / index limits
+  const long long rows = (long long)p->B * p->Hq * (((long long)p->T + 31) / 32);
+  if (rows > (1ll << 31) - 1) return LKL_ERR_TOO_LARGE;
+  return LKL_OK;
+}
+
+inline bool aligned(const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; }
+
+int32_t check_mask(const void* mask, int mdt) {
+  if (!mask) return LKL_OK;
+  const size_t es = mdt == LKL_MASK_I64 ? 8 : (mdt == LKL_MASK_I32 ? 4 : 1);
+  return aligned(mask, es) ? LKL_OK : LKL_ERR_MISALIGNED;
+}
+
+int32_t check_workspace(const lkl_problem* p, const void* mask, void* ws, size_t ws_bytes) {
+  const size_t need = lkl_workspace_size(p, mask != nullptr);
+  if (need == 0) return LKL_OK;
+  if (!ws || ws_bytes < need || !aligned(ws, 256)) return LKL_ERR_WORKSPACE;
+  return LKL_OK;
+}
+
+bool device_is_sm100() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return false;
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  return major == 10 && minor == 0;
+}
+
+bool use_tensor_cores(const Problem& q, const void* a, const void* b, const void* c,
+                      const void* d) {
+  if (g_force_generic.load()) return false;
+  if (!(aligned(a, 16) && aligned(b, 16) && aligned(c, 16) && aligned(d, 16))) return false;
+  return lkl::sm100_supports(q);
+}
+
+inline int32_t launch_status(cudaError_t e) { return e == cudaSuccess ? LKL_OK : LKL_ERR_LAUNCH; }
+
+// Packs the mask (if any) into the workspace; returns the bits pointer via *bits.
+int32_t prepare_mask(const lkl_problem* p, const void* mask, void* ws, uint32_t** bits,
+                     cudaStream_t st) {
+  *bits = nullptr;
+  if (!mask || p->B == 0 || p->T == 0) return LKL_OK;
+  *bits = static_cast<uint32_t*>(ws);
+  return launch_status(lkl::launch_pack_mask(mask, p->mask_dtype, p->B, p->T, *bits, st));
+}
+
+inline float* partials_ptr(const lkl_problem* p, const void* mask, void* ws) {
+  return reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + (mask ? bits_bytes(p) : 0));
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t lkl_abi_version(void) { return LKL_ABI_VERSION; }
+
+const char* lkl_status_string(int32_t s) {
+  switch (s) {
+    case LKL_OK: return "ok";
+    case LKL_ERR_NULL_POINTER: return "a required pointer is NULL";
+    case LKL_ERR_BAD_SHAPE: return "bad shape (B/T/H mismatch or Hq not divisible by Hkv)";
+    case LKL_ERR_BAD_HEAD_DIM: return "head dim is not in the supported set {8,16,32,64,128,256}";
+    case LKL_ERR_BAD_DTYPE: return "unsupported dtype";
+    case LKL_ERR_MISALIGNED: return "pointer not aligned to its element size";
+    case LKL_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+    case LKL_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case LKL_ERR_NO_DEVICE: return "no sm_100 CUDA device is current";
+    case LKL_ERR_DEVICE_TIMEOUT: return "a device-side bounded wait expired";
+    case LKL_ERR_BAD_ALIAS: return "dq == dk requires qs == ks and Hkv_s == Hq";
+    case LKL_ERR_TOO_LARGE: return "problem exceeds the supported size";
+    default: return "unknown status";
+  }
+}
+
+size_t lkl_workspace_size(const lkl_problem* p, int32_t has_mask) {
+  if (!p || p->B <= 0 || p->T <= 0 || p->Hq <= 0) return 0;
+  const Problem q = to_problem(p);
+  size_t n = round256((size_t)max_partials(q) * sizeof(float));
+  if (has_mask) n += bits_bytes(p);
+  return n;
+}
+
+int32_t lkl_lse(const void* q, const void* k, const void* mask, const lkl_problem* p, float* lse,
+                void* ws, size_t ws_bytes, void* stream) {
+  int32_t s = check_problem(p, false);
+  if (s) return s;
+  if (!q || !k || !lse) return LKL_ERR_NULL_POINTER;
+  if (!aligned(q, 2) || !aligned(k, 2) || !aligned(lse, 4)) return LKL_ERR_MISALIGNED;
+  if ((s = check_mask(mask, p->mask_dtype))) return s;
+  if (p->B == 0 || p->T == 0) return LKL_OK;
+  if ((s = check_workspace(p, mask, ws, ws_bytes))) return s;
+  if (!device_is_sm100()) return LKL_ERR_NO_DEVICE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t* bits;
+  if ((s = prepare_mask(p, mask, ws, &bits, st))) return s;
+  lkl_problem pp = *p;
+  pp.Hkv_t = p->Hkv_s;
+  pp.Dt = p->Ds;
+  pp.dtype_t = p->dtype_s;
+  const Problem qq = to_problem(&pp);
+  return launch_status(lkl::launch_generic_forward(0, qq, q, k, q, k, bits, lse, nullptr,
+                                                   nullptr, nullptr, st));
+}
+
+int32_t lkl_kl_forward(const void* qs, const void* ks, const float* lse_s, const void* qt,
+                       const void* kt, const float* lse_t, const void* mask,
+                       const lkl_problem* p, float* loss, void* ws, size_t ws_bytes,
+                       void* stream) {
+  int32_t s = check_problem(p, true);
+  if (s) return s;
+  if (!qs || !ks || !qt || !kt || !lse_s || !lse_t || !loss) return LKL_ERR_NULL_POINTER;
+  if (!aligned(qs, 2) || !aligned(ks, 2) || !aligned(qt, 2) || !aligned(kt, 2) ||
+      !aligned(lse_s, 4) || !aligned(lse_t, 4) || !aligned(loss, 4))
+    return LKL_ERR_MISALIGNED;
+  if ((s = check_mask(mask, p->mask_dtype))) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (p->B == 0 || p->T == 0) return launch_status(cudaMemsetAsync(loss, 0, sizeof(float), st));
+  if ((s = check_workspace(p, mask, ws, ws_bytes))) return s;
+  if (!device_is_sm100()) return LKL_ERR_NO_DEVICE;
+  uint32_t* bits;
+  if ((s = prepare_mask(p, mask, ws, &bits, st))) return s;
+  const Problem q = to_problem(p);
+  float* part = partials_ptr(p, mask, ws);
+  int np = 0;
+  cudaError_t e = lkl::launch_generic_forward(2, q, qs, ks, qt, kt, bits,
+                                              const_cast<float*>(lse_s),
+                                              const_cast<float*>(lse_t), part, &np, st);
+  if (e != cudaSuccess) return LKL_ERR_LAUNCH;
+  return launch_status(lkl::launch_reduce_partials(part, np, loss, st));
+}
+
+int32_t lkl_forward(const void* qs, const void* ks, const void* qt, const void* kt,
+                    const void* mask, const lkl_problem* p, float* lse_s, float* lse_t,
+                    float* loss, void* ws, size_t ws_bytes, void* stream) {
+  int32_t s = check_problem(p, true);
+  if (s) return s;
+  if (!qs || !ks || !qt || !kt || !lse_s || !lse_t || !loss) return LKL_ERR_NULL_POINTER;
+  if (!aligned(qs, 2) || !aligned(ks, 2) || !aligned(qt, 2) || !aligned(kt, 2) ||
+      !aligned(lse_s, 4) || !aligned(lse_t, 4) || !aligned(loss, 4))
+    return LKL_ERR_MISALIGNED;
+  if ((s = check_mask(mask, p->mask_dtype))) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (p->B == 0 || p->T == 0) return launch_status(cudaMemsetAsync(loss, 0, sizeof(float), st));
+  if ((s = check_workspace(p, mask, ws, ws_bytes))) return s;
+  if (!device_is_sm100()) return LKL_ERR_NO_DEVICE;
+  uint32_t* bits;
+  if ((s = prepare_mask(p, mask, ws, &bits, st))) return s;
+  const Problem q = to_problem(p);
+  float* part = partials_ptr(p, mask, ws);
+  int np = 0;
+  cudaError_t e;
+  if (use_tensor_cores(q, qs, ks, qt, kt)) {
+    t_last_path = 1;
+    e = lkl::launch_sm100_forward(q, qs, ks, qt, kt, bits, lse_s, lse_t, part, &np, st);
+  } else {
+    t_last_path = 0;
+    e = lkl::launch_generic_forward(1, q, qs, ks, qt, kt, bits, lse_s, lse_t, part, &np, st);
+  }
+  if (e != cudaSuccess) return LKL_ERR_LAUNCH;
+  return launch_status(lkl::launch_reduce_partials(part, np, loss, st));
+}
+
+int32_t lkl_backward(const void* qs, const void* ks, const float* lse_s, const void* qt,
+                     const void* kt, const float* lse_t, const void* mask, const lkl_problem* p,
+                     const float* dloss, float* dq, float* dk, void* ws, size_t ws_bytes,
+                     void* stream) {
+  int32_t s = check_problem(p, true);
+  if (s) return s;
+  if (!qs || !ks || !qt || !kt || !lse_s || !lse_t || !dq || !dk) return LKL_ERR_NULL_POINTER;
+  if (!aligned(qs, 2) || !aligned(ks, 2) || !aligned(qt, 2) || !aligned(kt, 2) ||
+      !aligned(lse_s, 4) || !aligned(lse_t, 4) || !aligned(dq, 16) || !aligned(dk, 16) ||
+      (dloss && !aligned(dloss, 4)))
+    return LKL_ERR_MISALIGNED;
+  if ((s = check_mask(mask, p->mask_dtype))) return s;
+  const bool alias = dq == dk;
+  if (alias && (qs != ks || p->Hkv_s != p->Hq)) return LKL_ERR_BAD_ALIAS;
+  if (p->B == 0 || p->T == 0) return LKL_OK;
+  if ((s = check_workspace(p, mask, ws, ws_bytes))) return s;
+  if (!device_is_sm100()) return LKL_ERR_NO_DEVICE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t* bits;
+  if ((s = prepare_mask(p, mask, ws, &bits, st))) return s;
+  const Problem q = to_problem(p);
+  // dk (and dq when it is the same buffer) accumulates with vector reductions
+  const size_t dk_bytes = (size_t)p->B * p->Hkv_s * p->T * p->Ds * sizeof(float);
+  if (cudaMemsetAsync(dk, 0, dk_bytes, st) != cudaSuccess) return LKL_ERR_LAUNCH;
+  cudaError_t e;
+  if (use_tensor_cores(q, qs, ks, qt, kt)) {
+    t_last_path = 1;
+    e = lkl::launch_sm100_backward(q, qs, ks, lse_s, qt, kt, lse_t, bits, dloss, dq, dk, alias, st);
+  } else {
+    t_last_path = 0;
+    e = lkl::launch_generic_backward(q, qs, ks, lse_s, qt, kt, lse_t, bits, dloss, dq, dk, alias,
+                                     st);
+  }
+  return launch_status(e);
+}
+
+int32_t lkl_device_status(void) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, lkl::g_device_error, sizeof(int)) != cudaSuccess)
+    return LKL_ERR_LAUNCH;
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(lkl::g_device_error, &zero, sizeof(int));
+    return LKL_ERR_DEVICE_TIMEOUT;
+  }
+  return LKL_OK;
+}
+
+int32_t lkl_last_path(void) { return t_last_path; }
+
+void lkl_set_force_generic(int32_t force) { g_force_generic.store(force ? 1 : 0); }
+
+}  // extern "C"

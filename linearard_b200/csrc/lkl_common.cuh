@@ -1,0 +1,95 @@
+// Shared device helpers for the attention-relation KL kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "linearard_b200.h"
+
+namespace lkl {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// Device-side error word, one per device that loads the library.  The bounded
+// waits of the tensor-core kernels set it instead of spinning forever.  The
+// library is one translation unit (liblinearard_b200.cu), so it is defined here.
+__device__ int g_device_error = 0;
+
+// Loads element `idx` of a fp16 / bf16 tensor as float.
+__device__ __forceinline__ float load_elem(const void* base, size_t idx, int dtype) {
+  if (dtype == LKL_BF16) {
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
+  }
+  return __half2float(reinterpret_cast<const __half*>(base)[idx]);
+}
+
+// Rounds a float through the tensor dtype (the reference casts the score
+// difference to the input dtype before the gradient dot, kernel_C.py:233).
+__device__ __forceinline__ float round_to_dtype(float v, int dtype) {
+  if (dtype == LKL_BF16) return __bfloat162float(__float2bfloat16_rn(v));
+  return __half2float(__float2half_rn(v));
+}
+
+// Nonzero test of one padding-mask element of any supported mask dtype.
+__device__ __forceinline__ bool mask_elem(const void* mask, size_t idx, int mdt) {
+  switch (mdt) {
+    case LKL_MASK_I32: return reinterpret_cast<const int32_t*>(mask)[idx] != 0;
+    case LKL_MASK_I64: return reinterpret_cast<const int64_t*>(mask)[idx] != 0;
+    default: return reinterpret_cast<const uint8_t*>(mask)[idx] != 0;
+  }
+}
+
+// Validity bit of token t of batch b in the packed [B][words] mask
+// (bit t%32 of word t/32).  `bits == nullptr` means every token is valid.
+__device__ __forceinline__ bool token_valid(const uint32_t* bits, int words, int b, int t) {
+  if (bits == nullptr) return true;
+  return (bits[(size_t)b * words + (t >> 5)] >> (t & 31)) & 1u;
+}
+
+}  // namespace lkl
+
+// Host-side launchers implemented in the .cu files.
+namespace lkl {
+
+struct Problem {
+  int B, Hq, Hkv_s, Hkv_t, T, Ds, Dt;
+  int dtype_s, dtype_t, causal;
+  float sc_s, sc_t;
+};
+
+// Packs a [B, T] mask into bit words; words = ceil(T/32).
+cudaError_t launch_pack_mask(const void* mask, int mdt, int B, int T, uint32_t* bits,
+                             cudaStream_t st);
+// Sums n partials in a fixed order into *out.
+cudaError_t launch_reduce_partials(const float* partials, int n, float* out, cudaStream_t st);
+
+// Generic CUDA-core kernels (any supported head dim).
+// mode 0: lse of the student pair only; 1: fused lse_s, lse_t, KL partials;
+// 2: KL partials from given lse_s/lse_t.
+cudaError_t launch_generic_forward(int mode, const Problem& p, const void* qs, const void* ks,
+                                   const void* qt, const void* kt, const uint32_t* bits,
+                                   float* lse_s, float* lse_t, float* partials,
+                                   int* num_partials, cudaStream_t st);
+cudaError_t launch_generic_backward(const Problem& p, const void* qs, const void* ks,
+                                    const float* lse_s, const void* qt, const void* kt,
+                                    const float* lse_t, const uint32_t* bits,
+                                    const float* dloss, float* dq, float* dk, bool alias,
+                                    cudaStream_t st);
+int generic_num_partials(const Problem& p);
+
+// sm_100a tensor-core kernels.
+bool sm100_supports(const Problem& p);
+int sm100_num_partials(const Problem& p);
+cudaError_t launch_sm100_forward(const Problem& p, const void* qs, const void* ks,
+                                 const void* qt, const void* kt, const uint32_t* bits,
+                                 float* lse_s, float* lse_t, float* partials,
+                                 int* num_partials, cudaStream_t st);
+cudaError_t launch_sm100_backward(const Problem& p, const void* qs, const void* ks,
+                                  const float* lse_s, const void* qt, const void* kt,
+                                  const float* lse_t, const uint32_t* bits, const float* dloss,
+                                  float* dq, float* dk, bool alias, cudaStream_t st);
+
+}  // namespace lkl

@@ -1,0 +1,699 @@
+// sm_100a tensor-core kernels for the attention-relation KL loss.
+//
+// Both kernels are row-stationary: one CTA owns a 128-row tile i of one
+// (batch, query head) and walks the 128-column tiles j <= i (all j when not
+// causal).  Operand tiles are staged by TMA (128-byte swizzle, no multicast),
+// scores are computed by tcgen05.mma into TMEM, and eight "row" warps (two
+// warpgroups, each owning 64 of the 128 columns of a tile for all 128 rows)
+// read them back with tcgen05.ld.
+//
+// Forward (replaces kernel_A x2 + kernel_B, kernel_A.py:42-159 / kernel_B.py:57-218):
+//   ss = Qs_i Ks_j^T, st = Qt_i Kt_j^T into a double-buffered TMEM pair; the
+//   row warps keep online (max, sum) for both and the teacher-weighted sum
+//   A = sum_j e^{st_j - m_t} (st_j - ss_j), so that
+//   KL_i = A / l_t + lse_s - lse_t   (exact: sum_j pt_j = 1).
+//
+// Backward (replaces kernel_C, kernel_C.py:63-261):
+//   recompute ss, st; D = e^{ss - lse_s} - e^{st - lse_t} rounded to the input
+//   dtype and written to shared memory in the UMMA K-major 128B-swizzled
+//   layout; then dq_i += D Ks_j (TMEM accumulator for the whole row tile) and
+//   dk_part = D^T Qs_i (same shared buffer read as MN-major), the latter
+//   drained by the row warps with vector fp32 reductions into dk.
+//
+// Warp roles (384 threads): warp 0 = TMA producer, warp 1 = MMA issuer and
+// TMEM owner, warps 2-3 idle, warps 4-11 = row warps (warp w reads TMEM
+// lanes 32*(w%4) .. +31).
+#include <math_constants.h>
+
+#include <mutex>
+
+#include "lkl_common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace lkl {
+namespace {
+
+using namespace sm100;
+
+constexpr int kBM = 128;          // rows per tile (= TMEM lanes)
+constexpr int kBN = 128;          // columns per tile
+constexpr int kChunk = 128 * 64 * 2;  // one [128 rows][64 elems] 16-bit swizzled chunk
+constexpr int kThreads = 384;
+constexpr int kMaxDynSmem = 232448;
+constexpr int kMisc = 1024;
+constexpr uint32_t kTmemCols = 512;
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float lg2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void named_bar(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+template <int DS, int DT>
+struct FwdLayout {
+  static constexpr int QS = kBM * DS * 2, QT = kBM * DT * 2;
+  static constexpr int STAGE = kBN * (DS + DT) * 2;
+  static constexpr int STAT = 5 * kBM * 4;  // second warpgroup's row statistics
+  static constexpr int AVAIL = kMaxDynSmem - 1024 - kMisc - STAT - QS - QT;
+  static constexpr int NS = (AVAIL / STAGE) >= 4 ? 4 : (AVAIL / STAGE);
+  static constexpr int OFF_QS = 0, OFF_QT = QS, OFF_K = QS + QT;
+  static constexpr int OFF_MISC = OFF_K + NS * STAGE;
+  static constexpr int OFF_STAT = OFF_MISC + kMisc;
+  static constexpr int BYTES = 1024 + OFF_STAT + STAT;
+  static_assert(NS >= 2, "forward needs two K stages");
+};
+
+template <int DS, int DT>
+struct BwdLayout {
+  static constexpr int QS = kBM * DS * 2, QT = kBM * DT * 2, DEL = kBM * kBN * 2;
+  static constexpr int STAGE = kBN * (DS + DT) * 2;
+  static constexpr int AVAIL = kMaxDynSmem - 1024 - kMisc - QS - QT - DEL;
+  static constexpr int NS = (AVAIL / STAGE) >= 3 ? 3 : (AVAIL / STAGE);
+  static constexpr int OFF_QS = 0, OFF_QT = QS, OFF_DEL = QS + QT, OFF_K = QS + QT + DEL;
+  static constexpr int OFF_MISC = OFF_K + NS * STAGE;
+  static constexpr int BYTES = 1024 + OFF_MISC + kMisc;
+  static_assert(NS >= 2, "backward needs two K stages");
+};
+
+struct Misc {
+  uint64_t q_full;
+  uint64_t k_full[4];
+  uint64_t k_empty[4];
+  uint64_t s_full[2];
+  uint64_t s_empty[2];
+  uint64_t d_full;
+  uint64_t d_empty;
+  uint32_t tmem_base;
+  int abort;
+  float red[8];
+};
+static_assert(sizeof(Misc) <= kMisc, "misc region too small");
+
+struct Tile {
+  int b, h, hs, ht, mt, n_ct, bh;
+};
+
+__device__ __forceinline__ Tile tile_of(const Problem& p) {
+  Tile t;
+  const int n_mt = (p.T + kBM - 1) / kBM;
+  const int BH = p.B * p.Hq;
+  // longest (latest) row tiles first, across all heads
+  t.mt = n_mt - 1 - (int)(blockIdx.x / BH);
+  t.bh = (int)(blockIdx.x % BH);
+  t.b = t.bh / p.Hq;
+  t.h = t.bh % p.Hq;
+  t.hs = t.h / (p.Hq / p.Hkv_s);
+  t.ht = t.h / (p.Hq / p.Hkv_t);
+  const int n_ct_all = (p.T + kBN - 1) / kBN;
+  t.n_ct = p.causal ? min(t.mt + 1, n_ct_all) : n_ct_all;
+  return t;
+}
+
+// K-major SW128 operand: K-step kk (16 elements) of a tile stored as
+// [rows][64]-element chunks of 16 KB.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk) {
+  return desc_sw128(base + (uint32_t)((kk >> 2) * kChunk + (kk & 3) * 32), 16, 1024);
+}
+// MN-major SW128 operand: K-step kk = 16 rows of 128 B; MN chunks 16 KB apart.
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int kk) {
+  return desc_sw128(base + (uint32_t)(kk * 16 * 128), kChunk, 1024);
+}
+
+__device__ __forceinline__ void issue_tile_loads(void* dst, const CUtensorMap* map,
+                                                 uint64_t* bar, int D, int row, int z) {
+  for (int c = 0; c < D / 64; ++c)
+    tma_load_3d(static_cast<uint8_t*>(dst) + c * kChunk, map, bar, c * 64, row, z);
+}
+
+template <typename Layout>
+__device__ __forceinline__ void setup_cta(Misc* misc, int warp, int lane) {
+  if (threadIdx.x == 0) {
+    mbar_init(&misc->q_full, 1);
+    for (int s = 0; s < 4; ++s) {
+      mbar_init(&misc->k_full[s], 1);
+      mbar_init(&misc->k_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&misc->s_full[s], 1);
+      mbar_init(&misc->s_empty[s], 8);
+    }
+    mbar_init(&misc->d_full, 8);
+    mbar_init(&misc->d_empty, 1);
+    misc->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&misc->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+}
+
+// ============================================================== forward
+template <int DS, int DT>
+__global__ void __launch_bounds__(kThreads, 1)
+sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs,
+                     const __grid_constant__ CUtensorMap tm_ks,
+                     const __grid_constant__ CUtensorMap tm_qt,
+                     const __grid_constant__ CUtensorMap tm_kt, const Problem p,
+                     const uint32_t* __restrict__ bits, float* __restrict__ lse_s,
+                     float* __restrict__ lse_t, float* __restrict__ partials) {
+  using L = FwdLayout<DS, DT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  Misc* misc = reinterpret_cast<Misc*>(smem + L::OFF_MISC);
+  float(*stat)[kBM] = reinterpret_cast<float(*)[kBM]>(smem + L::OFF_STAT);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Tile t = tile_of(p);
+  int* err = &g_device_error;
+  volatile int* abort = &misc->abort;
+
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_qs);
+    tma_prefetch_desc(&tm_ks);
+    tma_prefetch_desc(&tm_qt);
+    tma_prefetch_desc(&tm_kt);
+  }
+  setup_cta<L>(misc, warp, lane);
+  const uint32_t tmem = misc->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      mbar_arrive_expect_tx(&misc->q_full, L::QS + L::QT);
+      issue_tile_loads(smem + L::OFF_QS, &tm_qs, &misc->q_full, DS, t.mt * kBM, t.bh);
+      issue_tile_loads(smem + L::OFF_QT, &tm_qt, &misc->q_full, DT, t.mt * kBM, t.bh);
+      const int zs = t.b * p.Hkv_s + t.hs, zt = t.b * p.Hkv_t + t.ht;
+      for (int j = 0; j < t.n_ct; ++j) {
+        const int s = j % L::NS;
+        if (j >= L::NS && !mbar_wait(&misc->k_empty[s], ((j / L::NS) - 1) & 1, abort, err)) break;
+        uint8_t* st = smem + L::OFF_K + s * L::STAGE;
+        mbar_arrive_expect_tx(&misc->k_full[s], L::STAGE);
+        issue_tile_loads(st, &tm_ks, &misc->k_full[s], DS, j * kBN, zs);
+        issue_tile_loads(st + kBN * DS * 2, &tm_kt, &misc->k_full[s], DT, j * kBN, zt);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      const uint32_t id_s = idesc_f16(kBM, kBN, p.dtype_s, p.dtype_s, 0, 0);
+      const uint32_t id_t = idesc_f16(kBM, kBN, p.dtype_t, p.dtype_t, 0, 0);
+      const uint32_t a_s = smem_u32(smem + L::OFF_QS), a_t = smem_u32(smem + L::OFF_QT);
+      if (mbar_wait(&misc->q_full, 0, abort, err)) {
+        for (int j = 0; j < t.n_ct; ++j) {
+          const int s = j % L::NS, bf = j & 1;
+          if (!mbar_wait(&misc->k_full[s], (j / L::NS) & 1, abort, err)) break;
+          if (j >= 2 && !mbar_wait(&misc->s_empty[bf], ((j >> 1) - 1) & 1, abort, err)) break;
+          tc_fence_after();
+          const uint32_t b_s = smem_u32(smem + L::OFF_K + s * L::STAGE);
+          const uint32_t b_t = b_s + kBN * DS * 2;
+          const uint32_t d = tmem + bf * 256;
+#pragma unroll
+          for (int kk = 0; kk < DS / 16; ++kk)
+            umma_f16_ss(d, kmajor_desc(a_s, kk), kmajor_desc(b_s, kk), id_s, kk > 0);
+#pragma unroll
+          for (int kk = 0; kk < DT / 16; ++kk)
+            umma_f16_ss(d + 128, kmajor_desc(a_t, kk), kmajor_desc(b_t, kk), id_t, kk > 0);
+          umma_commit(&misc->k_empty[s]);
+          umma_commit(&misc->s_full[bf]);
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- row warps
+    const int wg = (warp - 4) >> 2, q = warp & 3;
+    const int r = q * 32 + lane;
+    const int i = t.mt * kBM + r;
+    const int words = (p.T + 31) >> 5;
+    const bool row_in = i < p.T;
+    const bool row_valid = row_in && token_valid(bits, words, t.b, i);
+    const int lim = p.causal ? min(i, p.T - 1) : p.T - 1;
+    const float cs = p.sc_s * kLog2e, ct = p.sc_t * kLog2e;
+    float m_s = -CUDART_INF_F, l_s = 0.f, m_t = -CUDART_INF_F, l_t = 0.f, acc = 0.f;
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+
+    for (int j = 0; j < t.n_ct; ++j) {
+      const int bf = j & 1;
+      if (!mbar_wait(&misc->s_full[bf], (j >> 1) & 1, abort, err)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float x[32], y[32];
+        const uint32_t col = bf * 256 + wg * 64 + half * 32;
+        tmem_ld32(lane_addr + col, x);
+        tmem_ld32(lane_addr + col + 128, y);
+        tmem_wait_ld();
+        if (half == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&misc->s_empty[bf]);
+        }
+        if (!row_valid) continue;
+        const int c0 = j * kBN + wg * 64 + half * 32;
+        const bool full = (c0 + 31 <= lim) && (bits == nullptr);
+        if (!full) {
+          // mask invalid columns: ss, st -> -inf, and keep the difference finite
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            const int c = c0 + k;
+            const bool ok = (c <= lim) && token_valid(bits, words, t.b, c);
+            if (!ok) {
+              x[k] = -CUDART_INF_F;
+              y[k] = -CUDART_INF_F;
+            }
+          }
+        }
+        float mx = -CUDART_INF_F, my = -CUDART_INF_F;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          mx = fmaxf(mx, x[k]);
+          my = fmaxf(my, y[k]);
+        }
+        if (my == -CUDART_INF_F) continue;  // no valid column in this chunk
+        const float ms_new = fmaxf(m_s, mx * cs);
+        const float mt_new = fmaxf(m_t, my * ct);
+        l_s *= ex2(m_s - ms_new);
+        const float beta = ex2(m_t - mt_new);
+        l_t *= beta;
+        acc *= beta;
+        float ls0 = 0.f, ls1 = 0.f, lt0 = 0.f, lt1 = 0.f, a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int k = 0; k < 32; k += 2) {
+          const float ps0 = ex2(fmaf(x[k], cs, -ms_new));
+          const float ps1 = ex2(fmaf(x[k + 1], cs, -ms_new));
+          const float pt0 = ex2(fmaf(y[k], ct, -mt_new));
+          const float pt1 = ex2(fmaf(y[k + 1], ct, -mt_new));
+          ls0 += ps0;
+          ls1 += ps1;
+          lt0 += pt0;
+          lt1 += pt1;
+          // pt * (st - ss); masked entries have pt = 0 and a finite stand-in difference
+          const float d0 = (pt0 > 0.f) ? fmaf(y[k], p.sc_t, -x[k] * p.sc_s) : 0.f;
+          const float d1 = (pt1 > 0.f) ? fmaf(y[k + 1], p.sc_t, -x[k + 1] * p.sc_s) : 0.f;
+          a0 = fmaf(pt0, d0, a0);
+          a1 = fmaf(pt1, d1, a1);
+        }
+        l_s += ls0 + ls1;
+        l_t += lt0 + lt1;
+        acc += a0 + a1;
+        m_s = ms_new;
+        m_t = mt_new;
+      }
+    }
+
+    // combine the two warpgroups' statistics of each row
+    if (wg == 1) {
+      stat[0][r] = m_s;
+      stat[1][r] = l_s;
+      stat[2][r] = m_t;
+      stat[3][r] = l_t;
+      stat[4][r] = acc;
+    }
+    named_bar(1, 256);
+    if (wg == 0) {
+      const float m_s2 = stat[0][r], l_s2 = stat[1][r];
+      const float m_t2 = stat[2][r], l_t2 = stat[3][r], acc2 = stat[4][r];
+      const float Ms = fmaxf(m_s, m_s2), Mt = fmaxf(m_t, m_t2);
+      float Ls = 0.f, Lt = 0.f, A = 0.f;
+      if (Ms != -CUDART_INF_F) Ls = l_s * ex2(m_s - Ms) + l_s2 * ex2(m_s2 - Ms);
+      if (Mt != -CUDART_INF_F) {
+        const float f1 = ex2(m_t - Mt), f2 = ex2(m_t2 - Mt);
+        Lt = l_t * f1 + l_t2 * f2;
+        A = acc * f1 + acc2 * f2;
+      }
+      const float lse_sv = (Ls > 0.f) ? (Ms + lg2(Ls)) * kLn2 : -CUDART_INF_F;
+      const float lse_tv = (Lt > 0.f) ? (Mt + lg2(Lt)) * kLn2 : -CUDART_INF_F;
+      float kl = 0.f;
+      if (row_valid && Ls > 0.f && Lt > 0.f) kl = A / Lt + lse_sv - lse_tv;
+      if (row_in) {
+        const size_t o = (size_t)t.bh * p.T + i;
+        lse_s[o] = row_valid ? lse_sv : 0.f;
+        lse_t[o] = row_valid ? lse_tv : 0.f;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) kl += __shfl_xor_sync(0xffffffffu, kl, o);
+      if (lane == 0) misc->red[q] = kl;
+      named_bar(2, 128);
+      if (q == 0 && lane == 0)
+        partials[blockIdx.x] = (misc->red[0] + misc->red[1]) + (misc->red[2] + misc->red[3]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ============================================================== backward
+__device__ __forceinline__ uint32_t pack2(float a, float b, int bf16) {
+  if (bf16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <int DS>
+__device__ __forceinline__ void drain_rows(uint32_t taddr, float* row_ptr, float scale,
+                                           bool do_store, bool atomic) {
+  // DS/2 fp32 columns of this thread's TMEM lane -> row_ptr[0 .. DS/2)
+#pragma unroll
+  for (int c = 0; c < DS / 2; c += 32) {
+    float v[32];
+    tmem_ld32(taddr + c, v);
+    tmem_wait_ld();
+    if (do_store) {
+#pragma unroll
+      for (int k = 0; k < 32; k += 4) {
+        float4 f = make_float4(v[k] * scale, v[k + 1] * scale, v[k + 2] * scale, v[k + 3] * scale);
+        float4* dst = reinterpret_cast<float4*>(row_ptr + c + k);
+        if (atomic) atomicAdd(dst, f);
+        else *dst = f;
+      }
+    }
+  }
+}
+
+template <int DS, int DT>
+__global__ void __launch_bounds__(kThreads, 1)
+sm100_backward_kernel(const __grid_constant__ CUtensorMap tm_qs,
+                      const __grid_constant__ CUtensorMap tm_ks,
+                      const __grid_constant__ CUtensorMap tm_qt,
+                      const __grid_constant__ CUtensorMap tm_kt, const Problem p,
+                      const float* __restrict__ lse_s, const float* __restrict__ lse_t,
+                      const uint32_t* __restrict__ bits, const float* __restrict__ dloss,
+                      float* dq, float* dk, int alias) {
+  using L = BwdLayout<DS, DT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  Misc* misc = reinterpret_cast<Misc*>(smem + L::OFF_MISC);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Tile t = tile_of(p);
+  int* err = &g_device_error;
+  volatile int* abort = &misc->abort;
+  constexpr uint32_t kColDq = 256, kColDk = 256 + DS;
+
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_qs);
+    tma_prefetch_desc(&tm_ks);
+    tma_prefetch_desc(&tm_qt);
+    tma_prefetch_desc(&tm_kt);
+  }
+  setup_cta<L>(misc, warp, lane);
+  const uint32_t tmem = misc->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&misc->q_full, L::QS + L::QT);
+      issue_tile_loads(smem + L::OFF_QS, &tm_qs, &misc->q_full, DS, t.mt * kBM, t.bh);
+      issue_tile_loads(smem + L::OFF_QT, &tm_qt, &misc->q_full, DT, t.mt * kBM, t.bh);
+      const int zs = t.b * p.Hkv_s + t.hs, zt = t.b * p.Hkv_t + t.ht;
+      for (int j = 0; j < t.n_ct; ++j) {
+        const int s = j % L::NS;
+        if (j >= L::NS && !mbar_wait(&misc->k_empty[s], ((j / L::NS) - 1) & 1, abort, err)) break;
+        uint8_t* st = smem + L::OFF_K + s * L::STAGE;
+        mbar_arrive_expect_tx(&misc->k_full[s], L::STAGE);
+        issue_tile_loads(st, &tm_ks, &misc->k_full[s], DS, j * kBN, zs);
+        issue_tile_loads(st + kBN * DS * 2, &tm_kt, &misc->k_full[s], DT, j * kBN, zt);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_s = idesc_f16(kBM, kBN, p.dtype_s, p.dtype_s, 0, 0);
+      const uint32_t id_t = idesc_f16(kBM, kBN, p.dtype_t, p.dtype_t, 0, 0);
+      const uint32_t id_dq = idesc_f16(kBM, DS, p.dtype_s, p.dtype_s, 0, 1);
+      const uint32_t id_dk = idesc_f16(kBN, DS, p.dtype_s, p.dtype_s, 1, 1);
+      const uint32_t a_s = smem_u32(smem + L::OFF_QS), a_t = smem_u32(smem + L::OFF_QT);
+      const uint32_t a_d = smem_u32(smem + L::OFF_DEL);
+      auto issue_scores = [&](int j) {
+        const int s = j % L::NS;
+        const uint32_t b_s = smem_u32(smem + L::OFF_K + s * L::STAGE);
+        const uint32_t b_t = b_s + kBN * DS * 2;
+#pragma unroll
+        for (int kk = 0; kk < DS / 16; ++kk)
+          umma_f16_ss(tmem, kmajor_desc(a_s, kk), kmajor_desc(b_s, kk), id_s, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < DT / 16; ++kk)
+          umma_f16_ss(tmem + 128, kmajor_desc(a_t, kk), kmajor_desc(b_t, kk), id_t, kk > 0);
+        umma_commit(&misc->s_full[0]);
+      };
+      bool ok = mbar_wait(&misc->q_full, 0, abort, err) &&
+                mbar_wait(&misc->k_full[0], 0, abort, err);
+      if (ok) {
+        tc_fence_after();
+        issue_scores(0);
+      }
+      for (int j = 0; ok && j < t.n_ct; ++j) {
+        if (j + 1 < t.n_ct) {
+          const int s1 = (j + 1) % L::NS;
+          if (!mbar_wait(&misc->k_full[s1], ((j + 1) / L::NS) & 1, abort, err)) break;
+          if (!mbar_wait(&misc->s_empty[0], j & 1, abort, err)) break;
+          tc_fence_after();
+          issue_scores(j + 1);
+        }
+        if (!mbar_wait(&misc->d_full, j & 1, abort, err)) break;
+        tc_fence_after();
+        const int s = j % L::NS;
+        const uint32_t b_s = smem_u32(smem + L::OFF_K + s * L::STAGE);
+        // dq(i, :) += D(i, j) Ks(j, :)     A = D K-major, B = Ks MN-major
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          umma_f16_ss(tmem + kColDq, kmajor_desc(a_d, kk), mnmajor_desc(b_s, kk), id_dq,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        // dk_part(j, :) = D(i, j)^T Qs(i, :)  A = D MN-major, B = Qs MN-major
+#pragma unroll
+        for (int kk = 0; kk < kBM / 16; ++kk)
+          umma_f16_ss(tmem + kColDk, mnmajor_desc(a_d, kk), mnmajor_desc(a_s, kk), id_dk,
+                      kk > 0 ? 1u : 0u);
+        umma_commit(&misc->d_empty);
+        umma_commit(&misc->k_empty[s]);
+      }
+    }
+  } else if (warp >= 4) {
+    const int wg = (warp - 4) >> 2, q = warp & 3;
+    const int r = q * 32 + lane;
+    const int i = t.mt * kBM + r;
+    const int words = (p.T + 31) >> 5;
+    const bool row_in = i < p.T;
+    float Ls = 0.f, Lt = 0.f;
+    bool row_ok = row_in && token_valid(bits, words, t.b, i);
+    if (row_in) {
+      Ls = lse_s[(size_t)t.bh * p.T + i];
+      Lt = lse_t[(size_t)t.bh * p.T + i];
+      row_ok = row_ok && isfinite(Ls) && isfinite(Lt);
+    }
+    const float Ls2 = Ls * kLog2e, Lt2 = Lt * kLog2e;
+    const int lim = p.causal ? min(i, p.T - 1) : p.T - 1;
+    const float cs = p.sc_s * kLog2e, ct = p.sc_t * kLog2e;
+    const float gscale = p.sc_s * (dloss ? *dloss : 1.f);
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+    uint8_t* del_row = smem + L::OFF_DEL + wg * kChunk + r * 128;
+    const int bf16 = p.dtype_s == LKL_BF16;
+    float* dk_head = dk + ((size_t)t.b * p.Hkv_s + t.hs) * (size_t)p.T * DS;
+
+    for (int j = 0; j < t.n_ct; ++j) {
+      if (!mbar_wait(&misc->s_full[0], j & 1, abort, err)) break;
+      tc_fence_after();
+      uint32_t packed[32];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float x[32], y[32];
+        const uint32_t col = wg * 64 + half * 32;
+        tmem_ld32(lane_addr + col, x);
+        tmem_ld32(lane_addr + 128 + col, y);
+        tmem_wait_ld();
+        if (half == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&misc->s_empty[0]);
+        }
+        const int c0 = j * kBN + wg * 64 + half * 32;
+        const bool full = row_ok && (c0 + 31 <= lim) && (bits == nullptr);
+#pragma unroll
+        for (int k = 0; k < 32; k += 2) {
+          float d0 = ex2(fmaf(x[k], cs, -Ls2)) - ex2(fmaf(y[k], ct, -Lt2));
+          float d1 = ex2(fmaf(x[k + 1], cs, -Ls2)) - ex2(fmaf(y[k + 1], ct, -Lt2));
+          if (!full) {
+            const int c = c0 + k;
+            const bool ok0 = row_ok && (c <= lim) && token_valid(bits, words, t.b, c);
+            const bool ok1 = row_ok && (c + 1 <= lim) && token_valid(bits, words, t.b, c + 1);
+            d0 = ok0 ? d0 : 0.f;
+            d1 = ok1 ? d1 : 0.f;
+          }
+          packed[half * 16 + (k >> 1)] = pack2(d0, d1, bf16);
+        }
+      }
+      if (j > 0) {
+        if (!mbar_wait(&misc->d_empty, (j - 1) & 1, abort, err)) break;
+        tc_fence_after();
+        const int jr = (j - 1) * kBN + r;
+        drain_rows<DS>(lane_addr + kColDk + wg * (DS / 2), dk_head + (size_t)jr * DS + wg * (DS / 2),
+                       gscale, jr < p.T, true);
+      }
+      // D row r, 64 columns of chunk wg: 8 x 16 B pieces, 128B-swizzled
+#pragma unroll
+      for (int pc = 0; pc < 8; ++pc) {
+        uint4 v = make_uint4(packed[pc * 4], packed[pc * 4 + 1], packed[pc * 4 + 2],
+                             packed[pc * 4 + 3]);
+        *reinterpret_cast<uint4*>(del_row + ((pc ^ (r & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&misc->d_full);
+    }
+    if (t.n_ct > 0 && mbar_wait(&misc->d_empty, (t.n_ct - 1) & 1, abort, err)) {
+      tc_fence_after();
+      const int jr = (t.n_ct - 1) * kBN + r;
+      drain_rows<DS>(lane_addr + kColDk + wg * (DS / 2), dk_head + (size_t)jr * DS + wg * (DS / 2),
+                     gscale, jr < p.T, true);
+      float* dq_row = dq + ((size_t)t.bh * p.T + i) * DS + wg * (DS / 2);
+      drain_rows<DS>(lane_addr + kColDq + wg * (DS / 2), dq_row, gscale, row_in, alias != 0);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ============================================================== host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// [BH][T][D] 16-bit tensor viewed as a 3-D map with a {64, 128, 1} box.
+bool make_map(CUtensorMap* m, const void* ptr, int dtype, int D, int T, int BH) {
+  EncodeTiledFn enc = get_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)BH};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)T * D * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, dtype == LKL_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                   3, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <typename K>
+cudaError_t prep(K kernel, int bytes) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+struct Maps {
+  CUtensorMap qs, ks, qt, kt;
+};
+
+bool build_maps(Maps& m, const Problem& p, const void* qs, const void* ks, const void* qt,
+                const void* kt) {
+  return make_map(&m.qs, qs, p.dtype_s, p.Ds, p.T, p.B * p.Hq) &&
+         make_map(&m.ks, ks, p.dtype_s, p.Ds, p.T, p.B * p.Hkv_s) &&
+         make_map(&m.qt, qt, p.dtype_t, p.Dt, p.T, p.B * p.Hq) &&
+         make_map(&m.kt, kt, p.dtype_t, p.Dt, p.T, p.B * p.Hkv_t);
+}
+
+template <int DS, int DT>
+cudaError_t run_forward(const Problem& p, const Maps& m, const uint32_t* bits, float* lse_s,
+                        float* lse_t, float* partials, cudaStream_t st) {
+  using L = FwdLayout<DS, DT>;
+  auto k = sm100_forward_kernel<DS, DT>;
+  cudaError_t e = prep(k, L::BYTES);
+  if (e != cudaSuccess) return e;
+  const int grid = sm100_num_partials(p);
+  k<<<grid, kThreads, L::BYTES, st>>>(m.qs, m.ks, m.qt, m.kt, p, bits, lse_s, lse_t, partials);
+  return cudaGetLastError();
+}
+
+template <int DS, int DT>
+cudaError_t run_backward(const Problem& p, const Maps& m, const float* lse_s, const float* lse_t,
+                         const uint32_t* bits, const float* dloss, float* dq, float* dk,
+                         bool alias, cudaStream_t st) {
+  using L = BwdLayout<DS, DT>;
+  auto k = sm100_backward_kernel<DS, DT>;
+  cudaError_t e = prep(k, L::BYTES);
+  if (e != cudaSuccess) return e;
+  const int grid = sm100_num_partials(p);
+  k<<<grid, kThreads, L::BYTES, st>>>(m.qs, m.ks, m.qt, m.kt, p, lse_s, lse_t, bits, dloss, dq,
+                                       dk, alias ? 1 : 0);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool sm100_supports(const Problem& p) {
+  const bool ds_ok = p.Ds == 64 || p.Ds == 128;
+  const bool dt_ok = p.Dt == 64 || p.Dt == 128;
+  return ds_ok && dt_ok && p.sc_s > 0.f && p.sc_t > 0.f && p.T >= 1 && get_encoder() != nullptr;
+}
+
+int sm100_num_partials(const Problem& p) { return p.B * p.Hq * ((p.T + kBM - 1) / kBM); }
+
+cudaError_t launch_sm100_forward(const Problem& p, const void* qs, const void* ks,
+                                 const void* qt, const void* kt, const uint32_t* bits,
+                                 float* lse_s, float* lse_t, float* partials,
+                                 int* num_partials, cudaStream_t st) {
+  Maps m;
+  if (!build_maps(m, p, qs, ks, qt, kt)) return cudaErrorInvalidValue;
+  if (num_partials) *num_partials = sm100_num_partials(p);
+  if (p.Ds == 128 && p.Dt == 128) return run_forward<128, 128>(p, m, bits, lse_s, lse_t, partials, st);
+  if (p.Ds == 64 && p.Dt == 64) return run_forward<64, 64>(p, m, bits, lse_s, lse_t, partials, st);
+  if (p.Ds == 128 && p.Dt == 64) return run_forward<128, 64>(p, m, bits, lse_s, lse_t, partials, st);
+  return run_forward<64, 128>(p, m, bits, lse_s, lse_t, partials, st);
+}
+
+cudaError_t launch_sm100_backward(const Problem& p, const void* qs, const void* ks,
+                                  const float* lse_s, const void* qt, const void* kt,
+                                  const float* lse_t, const uint32_t* bits, const float* dloss,
+                                  float* dq, float* dk, bool alias, cudaStream_t st) {
+  Maps m;
+  if (!build_maps(m, p, qs, ks, qt, kt)) return cudaErrorInvalidValue;
+  if (p.Ds == 128 && p.Dt == 128)
+    return run_backward<128, 128>(p, m, lse_s, lse_t, bits, dloss, dq, dk, alias, st);
+  if (p.Ds == 64 && p.Dt == 64)
+    return run_backward<64, 64>(p, m, lse_s, lse_t, bits, dloss, dq, dk, alias, st);
+  if (p.Ds == 128 && p.Dt == 64)
+    return run_backward<128, 64>(p, m, lse_s, lse_t, bits, dloss, dq, dk, alias, st);
+  return run_backward<64, 128>(p, m, lse_s, lse_t, bits, dloss, dq, dk, alias, st);
+}
+
+}  // namespace lkl

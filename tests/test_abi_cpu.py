@@ -1,0 +1,131 @@
+"""C-ABI checks that need no GPU: the library loads, exports every function
+that include/linearard_b200.h declares, and rejects bad arguments with the
+documented status codes before touching the device."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from linearard_b200 import _lib
+from linearard_b200.attention_KL import _common
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "linearard_b200.h")
+
+
+def header_functions():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:[\w\s\*]+?)\b(lkl_\w+)\s*\(", src, re.M)))
+
+
+def test_library_loads_and_exports_header_symbols():
+    L = _lib.lib()
+    names = header_functions()
+    assert len(names) >= 10
+    assert set(names) == set(_lib.EXPORTS)
+    for n in names:
+        assert hasattr(L, n), n
+    assert L.lkl_abi_version() == 1
+
+
+def test_status_strings():
+    L = _lib.lib()
+    for code in range(12):
+        assert L.lkl_status_string(code)
+    assert L.lkl_status_string(0) == b"ok"
+
+
+def _prob(**kw):
+    d = dict(B=1, Hq=4, Hkv_s=2, Hkv_t=4, T=300, Ds=128, Dt=128, dtype_s=1, dtype_t=1,
+             causal=1, mask_dtype=2, sm_scale_s=0.0, sm_scale_t=0.0)
+    d.update(kw)
+    return _lib.LKLProblem(**d)
+
+
+def test_workspace_size():
+    L = _lib.lib()
+    p = _prob()
+    n0 = L.lkl_workspace_size(ctypes.byref(p), 0)
+    n1 = L.lkl_workspace_size(ctypes.byref(p), 1)
+    assert n0 % 256 == 0 and n1 % 256 == 0
+    # one fp32 partial per 32-row block of each (batch, head)
+    assert n0 >= 4 * 1 * 4 * ((300 + 31) // 32)
+    assert n1 - n0 >= 1 * ((300 + 31) // 32) * 4
+    assert L.lkl_workspace_size(ctypes.byref(_prob(T=0)), 1) == 0
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(Hq=6, Hkv_s=4), 2),       # Hq % Hkv_s
+    (dict(Hkv_t=3), 2),             # Hq % Hkv_t
+    (dict(Ds=96), 3),               # head dim
+    (dict(Dt=512), 3),
+    (dict(dtype_s=7), 4),
+    (dict(mask_dtype=9), 4),
+    (dict(B=-1), 2),
+])
+def test_bad_problem_rejected_before_device(kw, code):
+    L = _lib.lib()
+    p = _prob(**kw)
+    fake = ctypes.c_void_p(0x10000)
+    st = L.lkl_forward(fake, fake, fake, fake, None, ctypes.byref(p), fake, fake, fake,
+                       fake, 1 << 20, None)
+    assert st == code, _lib.STATUS.get(st)
+
+
+def test_null_pointers_and_alias_rules():
+    L = _lib.lib()
+    p = _prob(Hkv_s=4)
+    fake = ctypes.c_void_p(0x10000)
+    other = ctypes.c_void_p(0x20000)
+    assert L.lkl_forward(None, fake, fake, fake, None, ctypes.byref(p), fake, fake, fake,
+                         fake, 1 << 20, None) == 1
+    # dq == dk but qs != ks -> bad alias
+    assert L.lkl_backward(fake, other, fake, fake, fake, fake, None, ctypes.byref(p), None,
+                          fake, fake, fake, 1 << 20, None) == 10
+    # misaligned gradient buffer
+    odd = ctypes.c_void_p(0x10004)
+    assert L.lkl_backward(fake, fake, fake, fake, fake, fake, None, ctypes.byref(p), None,
+                          odd, fake, fake, 1 << 20, None) == 5
+
+
+def test_workspace_too_small_rejected():
+    L = _lib.lib()
+    p = _prob()
+    fake = ctypes.c_void_p(0x10000)
+    st = L.lkl_forward(fake, fake, fake, fake, None, ctypes.byref(p), fake, fake, fake,
+                       fake, 16, None)
+    assert st == 6
+
+
+def test_empty_sequence_is_not_an_error_for_lse():
+    L = _lib.lib()
+    p = _prob(T=0)
+    fake = ctypes.c_void_p(0x10000)
+    assert L.lkl_lse(fake, fake, None, ctypes.byref(p), fake, None, 0, None) == 0
+
+
+def test_python_wrappers_assert_like_reference():
+    """Same failure mode as the reference wrappers (AssertionError) on CPU tensors."""
+    from linearard_b200.attention_KL import attn_kl_align, lse_stats
+    q = torch.randn(1, 2, 8, 16, dtype=torch.float16)
+    with pytest.raises(AssertionError, match="must be on CUDA"):
+        lse_stats(q, q)
+    with pytest.raises(AssertionError):
+        attn_kl_align(q, q, q, q)
+
+
+def test_wrapper_has_no_tensor_math():
+    """The reference's static audit (test_kernel_A.py:102-119): wrapper sources
+    contain no torch math calls -- everything is computed by the library."""
+    import inspect
+    from linearard_b200.attention_KL import kernel_A, kernel_B, kernel_C, integration
+    banned = ["matmul", "einsum", "softmax", "logsumexp", "exp(", "log(", "sum(", "max(",
+              "mean(", "transpose"]
+    for fn in (kernel_A.lse_stats, kernel_B.kl_forward, kernel_C.kl_backward,
+               integration.attn_kl_forward, integration.AttnKLAlignFn.forward,
+               integration.AttnKLAlignFn.backward):
+        src = inspect.getsource(fn).lower()
+        for key in banned:
+            assert key not in src, f"{fn.__qualname__} contains {key}"
