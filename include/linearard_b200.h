@@ -139,6 +139,32 @@ int32_t lkl_last_path(void);
  * (0, the default); process-wide.  For parity tests that cross-check paths. */
 void lkl_set_force_generic(int32_t force);
 
+/* Size of the scratch array that lkl_forward_noalloc uses on each device. */
+#define LKL_NOALLOC_SCRATCH_BYTES (1u << 20)
+
+/* lkl_forward without a workspace argument and without any device allocation.
+ * No counterpart in the reference: LinearARD's wrappers always allocate their
+ * outputs and scratch through PyTorch.  This is for callers that cannot
+ * allocate device memory -- a C/Go/Java binding that only receives pointers
+ * from a framework owning the memory pool, or code that must not call
+ * cudaMalloc mid-step because it can synchronise the device.  The caller still
+ * passes every input and output (lse_s, lse_t, loss) exactly as for
+ * lkl_forward; the scratch comes from a fixed LKL_NOALLOC_SCRATCH_BYTES array
+ * inside the library, which every GPU that loads the library keeps until the
+ * process exits.
+ *  - Limit: problems whose lkl_workspace_size() exceeds LKL_NOALLOC_SCRATCH_BYTES
+ *    are refused with LKL_ERR_TOO_LARGE (use lkl_forward with a workspace).
+ *  - The first call on each device looks up the array's device address
+ *    (cudaGetSymbolAddress, with that device current); make that first call
+ *    before any stream capture.
+ *  - All calls on a device share the one array: calls that can overlap on the
+ *    GPU (different streams, or host threads without ordering) race on it and
+ *    must be serialised by the caller.  Each call rewrites every byte it
+ *    reads, so nothing needs clearing in between. */
+int32_t lkl_forward_noalloc(const void* qs, const void* ks, const void* qt, const void* kt,
+                            const void* mask, const lkl_problem* p,
+                            float* lse_s, float* lse_t, float* loss, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

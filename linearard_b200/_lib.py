@@ -29,7 +29,7 @@ MASK_DTYPES = {"bool": LKL_MASK_BOOL, "uint8": LKL_MASK_U8, "int32": LKL_MASK_I3
 # every symbol the header declares
 EXPORTS = ("lkl_abi_version", "lkl_status_string", "lkl_workspace_size", "lkl_lse",
            "lkl_kl_forward", "lkl_forward", "lkl_backward", "lkl_device_status",
-           "lkl_last_path", "lkl_set_force_generic")
+           "lkl_last_path", "lkl_set_force_generic", "lkl_forward_noalloc")
 
 
 class LKLProblem(ctypes.Structure):
@@ -74,6 +74,8 @@ def _declare(L):
     L.lkl_last_path.restype = _i32
     L.lkl_set_force_generic.restype = None
     L.lkl_set_force_generic.argtypes = [_i32]
+    L.lkl_forward_noalloc.restype = _i32
+    L.lkl_forward_noalloc.argtypes = [_vp, _vp, _vp, _vp, _vp, _P, _vp, _vp, _vp, _vp]
 
 
 def lib(path: str | None = None):

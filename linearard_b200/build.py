@@ -22,7 +22,7 @@ OUT_DIR = os.path.join(PKG, "_lib")
 LIB_NAME = "liblinearard_b200.so"
 LIB_PATH = os.path.join(OUT_DIR, LIB_NAME)
 
-SOURCES = ["liblinearard_b200.cu", "lkl_api.cu", "lkl_generic.cu", "lkl_sm100.cu",
+SOURCES = ["liblinearard_b200.cu", "lkl_api.cu", "lkl_generic.cu", "lkl_sm100.cu", "lkl_noalloc.cu",
            "lkl_common.cuh", "sm100_ptx.cuh"]
 
 NVCC_FLAGS = [

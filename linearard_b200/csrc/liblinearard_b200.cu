@@ -3,3 +3,4 @@
 #include "lkl_generic.cu"
 #include "lkl_sm100.cu"
 #include "lkl_api.cu"
+#include "lkl_noalloc.cu"

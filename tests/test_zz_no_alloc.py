@@ -1,0 +1,91 @@
+"""lkl_forward_noalloc: the fused forward for callers that cannot allocate.
+
+Some callers of this library cannot allocate device memory -- a C/Go/Java
+binding that only receives pointers from a framework owning the memory pool,
+or code that must not call cudaMalloc mid-step because it can synchronise the
+device.  lkl_forward_noalloc takes no workspace and uses a fixed scratch array
+inside the library instead.  These tests call it through the C ABI and check
+that it returns what lkl_forward (with a caller-provided workspace) returns, on
+two calls in a row, and that it refuses problems beyond its scratch size.
+
+The file is named so that pytest collects it last.
+"""
+import ctypes
+
+import pytest
+import torch
+
+from linearard_b200 import _lib
+
+LOSS_REL = 1e-3   # north-star loss tolerance used by every parity test
+LSE_TOL = 1e-4
+
+
+def _problem(B, Hq, Hkv, T, D, mask_dtype=_lib.LKL_MASK_I32):
+    return _lib.LKLProblem(B=B, Hq=Hq, Hkv_s=Hkv, Hkv_t=Hkv, T=T, Ds=D, Dt=D,
+                           dtype_s=_lib.LKL_BF16, dtype_t=_lib.LKL_BF16, causal=1,
+                           mask_dtype=mask_dtype, sm_scale_s=0.0, sm_scale_t=0.0)
+
+
+def _vp(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _inputs(seed, B, Hq, Hkv, T, D, with_mask):
+    g = torch.Generator().manual_seed(seed)
+    qs = torch.randn(B, Hq, T, D, generator=g).bfloat16().cuda()
+    ks = torch.randn(B, Hkv, T, D, generator=g).bfloat16().cuda()
+    qt = (qs.float().cpu() + 0.2 * torch.randn(B, Hq, T, D, generator=g)).bfloat16().cuda()
+    kt = torch.randn(B, Hkv, T, D, generator=g).bfloat16().cuda()
+    mask = None
+    if with_mask:
+        mask = (torch.rand(B, T, generator=g) > 0.3).to(torch.int32)
+        mask[:, 0] = 1
+        mask = mask.cuda()
+    return qs, ks, qt, kt, mask
+
+
+def _run(fn_name, args, prob, B, Hq, T):
+    L = _lib.lib()
+    lse_s = torch.empty(B, Hq, T, device="cuda")
+    lse_t = torch.empty(B, Hq, T, device="cuda")
+    loss = torch.empty((), device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    qs, ks, qt, kt, mask = args
+    if fn_name == "lkl_forward":
+        n = L.lkl_workspace_size(ctypes.byref(prob), 1 if mask is not None else 0)
+        ws = torch.empty(max(n, 256), dtype=torch.uint8, device="cuda")
+        st = L.lkl_forward(_vp(qs), _vp(ks), _vp(qt), _vp(kt), _vp(mask), ctypes.byref(prob),
+                           _vp(lse_s), _vp(lse_t), _vp(loss), _vp(ws), n, stream)
+    else:
+        st = L.lkl_forward_noalloc(_vp(qs), _vp(ks), _vp(qt), _vp(kt), _vp(mask),
+                                   ctypes.byref(prob), _vp(lse_s), _vp(lse_t), _vp(loss), stream)
+    assert st == 0, _lib.STATUS.get(st)
+    torch.cuda.synchronize()
+    return float(loss), lse_s, lse_t
+
+
+@pytest.mark.gpu
+def test_noalloc_matches_workspace_forward_two_calls():
+    # two different problems back to back: the second (with a padding mask and
+    # more tiles) must not see anything the first left in the shared scratch
+    cases = [(1, (1, 4, 2, 700, 128), False), (2, (2, 4, 4, 1300, 64), True)]
+    for seed, (B, Hq, Hkv, T, D), with_mask in cases:
+        args = _inputs(seed, B, Hq, Hkv, T, D, with_mask)
+        prob = _problem(B, Hq, Hkv, T, D)
+        ref_loss, ref_ls, ref_lt = _run("lkl_forward", args, prob, B, Hq, T)
+        loss, ls, lt = _run("lkl_forward_noalloc", args, prob, B, Hq, T)
+        assert abs(loss - ref_loss) <= LOSS_REL * abs(ref_loss), (loss, ref_loss)
+        torch.testing.assert_close(ls, ref_ls, rtol=LSE_TOL, atol=LSE_TOL)
+        torch.testing.assert_close(lt, ref_lt, rtol=LSE_TOL, atol=LSE_TOL)
+    assert _lib.lib().lkl_device_status() == 0
+
+
+def test_noalloc_refuses_problems_beyond_its_scratch():
+    """Refused with LKL_ERR_TOO_LARGE before any device work (no GPU needed)."""
+    L = _lib.lib()
+    prob = _problem(8, 64, 8, 1 << 20, 128)   # 8*64*32768 partials alone = 64 MiB
+    fake = ctypes.c_void_p(0x10000)
+    st = L.lkl_forward_noalloc(fake, fake, fake, fake, None, ctypes.byref(prob), fake, fake,
+                               fake, None)
+    assert st == 11, _lib.STATUS.get(st)
