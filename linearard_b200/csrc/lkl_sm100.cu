@@ -17,8 +17,9 @@
 //   recompute ss, st; D = e^{ss - lse_s} - e^{st - lse_t} rounded to the input
 //   dtype and written to shared memory in the UMMA K-major 128B-swizzled
 //   layout; then dq_i += D Ks_j (TMEM accumulator for the whole row tile) and
-//   dk_part = D^T Qs_i (same shared buffer read as MN-major), the latter
-//   drained by the row warps with vector fp32 reductions into dk.
+//   dk_part = D^T Qs_i (same shared buffer read as MN-major; for d = 128 its
+//   transpose Qs_i^T D, so that TMEM lanes are features), the latter drained
+//   by the row warps with fp32 reductions into dk.
 //
 // Warp roles (384 threads): warp 0 = TMA producer, warp 1 = MMA issuer and
 // TMEM owner, warps 2-3 idle, warps 4-11 = row warps (warp w reads TMEM
@@ -110,9 +111,12 @@ __device__ __forceinline__ Tile tile_of(const Problem& p) {
   Tile t;
   const int n_mt = (p.T + kBM - 1) / kBM;
   const int BH = p.B * p.Hq;
-  // longest (latest) row tiles first, across all heads
-  t.mt = n_mt - 1 - (int)(blockIdx.x / BH);
-  t.bh = (int)(blockIdx.x % BH);
+  // Head-major order, longest (latest) row tiles of each head first: the CTAs
+  // resident at any time work on one or two heads, so those heads' K tiles and
+  // gradient rows stay in L2 instead of every head's at once.
+  (void)BH;
+  t.bh = (int)(blockIdx.x / n_mt);
+  t.mt = n_mt - 1 - (int)(blockIdx.x % n_mt);
   t.b = t.bh / p.Hq;
   t.h = t.bh % p.Hq;
   t.hs = t.h / (p.Hq / p.Hkv_s);
@@ -393,6 +397,24 @@ __device__ __forceinline__ void drain_rows(uint32_t taddr, float* row_ptr, float
   }
 }
 
+// dk_part^T (TMEM lane = feature d, column = key row j) -> dk[j][d]: the 32
+// lanes of a warp are 32 consecutive features of one key row, so every
+// reduction instruction of the warp covers 128 contiguous bytes.
+__device__ __forceinline__ void drain_dkT(uint32_t taddr, float* dk_head, int j0, int d, int T,
+                                          int DS, float scale) {
+#pragma unroll
+  for (int c = 0; c < 64; c += 32) {
+    float v[32];
+    tmem_ld32(taddr + c, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      const int j = j0 + c + k;
+      if (j < T) atomicAdd(dk_head + (size_t)j * DS + d, v[k] * scale);
+    }
+  }
+}
+
 template <int DS, int DT>
 __global__ void __launch_bounds__(kThreads, 1)
 sm100_backward_kernel(const __grid_constant__ CUtensorMap tm_qs,
@@ -411,6 +433,7 @@ sm100_backward_kernel(const __grid_constant__ CUtensorMap tm_qs,
   int* err = &g_device_error;
   volatile int* abort = &misc->abort;
   constexpr uint32_t kColDq = 256, kColDk = 256 + DS;
+  constexpr bool kDkT = DS == 128;
 
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_qs);
@@ -441,7 +464,9 @@ sm100_backward_kernel(const __grid_constant__ CUtensorMap tm_qs,
       const uint32_t id_s = idesc_f16(kBM, kBN, p.dtype_s, p.dtype_s, 0, 0);
       const uint32_t id_t = idesc_f16(kBM, kBN, p.dtype_t, p.dtype_t, 0, 0);
       const uint32_t id_dq = idesc_f16(kBM, DS, p.dtype_s, p.dtype_s, 0, 1);
-      const uint32_t id_dk = idesc_f16(kBN, DS, p.dtype_s, p.dtype_s, 1, 1);
+      // DS == 128: dk_part^T = Qs^T D (M = d, N = j); otherwise dk_part = D^T Qs
+      const uint32_t id_dk = kDkT ? idesc_f16(DS, kBN, p.dtype_s, p.dtype_s, 1, 1)
+                                  : idesc_f16(kBN, DS, p.dtype_s, p.dtype_s, 1, 1);
       const uint32_t a_s = smem_u32(smem + L::OFF_QS), a_t = smem_u32(smem + L::OFF_QT);
       const uint32_t a_d = smem_u32(smem + L::OFF_DEL);
       auto issue_scores = [&](int j) {
@@ -479,11 +504,19 @@ sm100_backward_kernel(const __grid_constant__ CUtensorMap tm_qs,
         for (int kk = 0; kk < kBN / 16; ++kk)
           umma_f16_ss(tmem + kColDq, kmajor_desc(a_d, kk), mnmajor_desc(b_s, kk), id_dq,
                       (j > 0 || kk > 0) ? 1u : 0u);
-        // dk_part(j, :) = D(i, j)^T Qs(i, :)  A = D MN-major, B = Qs MN-major
+        if (kDkT) {
+          // dk_part^T(:, j) = Qs(i, :)^T D(i, j)  A = Qs MN-major, B = D MN-major
 #pragma unroll
-        for (int kk = 0; kk < kBM / 16; ++kk)
-          umma_f16_ss(tmem + kColDk, mnmajor_desc(a_d, kk), mnmajor_desc(a_s, kk), id_dk,
-                      kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < kBM / 16; ++kk)
+            umma_f16_ss(tmem + kColDk, mnmajor_desc(a_s, kk), mnmajor_desc(a_d, kk), id_dk,
+                        kk > 0 ? 1u : 0u);
+        } else {
+          // dk_part(j, :) = D(i, j)^T Qs(i, :)  A = D MN-major, B = Qs MN-major
+#pragma unroll
+          for (int kk = 0; kk < kBM / 16; ++kk)
+            umma_f16_ss(tmem + kColDk, mnmajor_desc(a_d, kk), mnmajor_desc(a_s, kk), id_dk,
+                        kk > 0 ? 1u : 0u);
+        }
         umma_commit(&misc->d_empty);
         umma_commit(&misc->k_empty[s]);
       }
@@ -545,9 +578,14 @@ sm100_backward_kernel(const __grid_constant__ CUtensorMap tm_qs,
       if (j > 0) {
         if (!mbar_wait(&misc->d_empty, (j - 1) & 1, abort, err)) break;
         tc_fence_after();
-        const int jr = (j - 1) * kBN + r;
-        drain_rows<DS>(lane_addr + kColDk + wg * (DS / 2), dk_head + (size_t)jr * DS + wg * (DS / 2),
-                       gscale, jr < p.T, true);
+        if (kDkT) {
+          drain_dkT(lane_addr + kColDk + wg * 64, dk_head, (j - 1) * kBN + wg * 64, r, p.T, DS,
+                    gscale);
+        } else {
+          const int jr = (j - 1) * kBN + r;
+          drain_rows<DS>(lane_addr + kColDk + wg * (DS / 2),
+                         dk_head + (size_t)jr * DS + wg * (DS / 2), gscale, jr < p.T, true);
+        }
       }
       // D row r, 64 columns of chunk wg: 8 x 16 B pieces, 128B-swizzled
 #pragma unroll
@@ -563,9 +601,14 @@ sm100_backward_kernel(const __grid_constant__ CUtensorMap tm_qs,
     }
     if (t.n_ct > 0 && mbar_wait(&misc->d_empty, (t.n_ct - 1) & 1, abort, err)) {
       tc_fence_after();
-      const int jr = (t.n_ct - 1) * kBN + r;
-      drain_rows<DS>(lane_addr + kColDk + wg * (DS / 2), dk_head + (size_t)jr * DS + wg * (DS / 2),
-                     gscale, jr < p.T, true);
+      if (kDkT) {
+        drain_dkT(lane_addr + kColDk + wg * 64, dk_head, (t.n_ct - 1) * kBN + wg * 64, r, p.T,
+                  DS, gscale);
+      } else {
+        const int jr = (t.n_ct - 1) * kBN + r;
+        drain_rows<DS>(lane_addr + kColDk + wg * (DS / 2),
+                       dk_head + (size_t)jr * DS + wg * (DS / 2), gscale, jr < p.T, true);
+      }
       float* dq_row = dq + ((size_t)t.bh * p.T + i) * DS + wg * (DS / 2);
       drain_rows<DS>(lane_addr + kColDq + wg * (DS / 2), dq_row, gscale, row_in, alias != 0);
     }
