@@ -24,7 +24,10 @@
  *    bf16 (last stride 1), lse tensors contiguous fp32 [B, Hq, T].
  *  - mask: NULL (no padding) or a device pointer to a contiguous [B, T] array
  *    of LKL_MASK_* elements, nonzero = valid token.
- *  - All work is enqueued on `stream`; nothing synchronises the host.
+ *  - Each entry point makes the device that owns its first q pointer current
+ *    on the calling thread (cudaSetDevice) before any work; `stream` must
+ *    belong to that device.  All work is enqueued on `stream`; nothing
+ *    synchronises the host.
  *  - Scratch memory is caller-provided (`workspace`, `workspace_bytes`); query
  *    the size with lkl_workspace_size().  The library never allocates.
  *  - Return value: LKL_OK or an LKL_ERR_* code; lkl_status_string() names it.
@@ -134,6 +137,10 @@ int32_t lkl_device_status(void);
  * thread dispatched to: 1 = sm_100a tensor-core kernels, 0 = generic CUDA-core
  * kernels (head dims or alignments the tensor-core kernels do not cover). */
 int32_t lkl_last_path(void);
+
+/* cudaError_t value (as int) of the last CUDA call that made an entry point on
+ * this host thread return LKL_ERR_LAUNCH; 0 if none.  Diagnostic only. */
+int32_t lkl_last_cuda_error(void);
 
 /* Force the generic CUDA-core kernels (nonzero) or allow the tensor-core path
  * (0, the default); process-wide.  For parity tests that cross-check paths. */

@@ -29,7 +29,8 @@ MASK_DTYPES = {"bool": LKL_MASK_BOOL, "uint8": LKL_MASK_U8, "int32": LKL_MASK_I3
 # every symbol the header declares
 EXPORTS = ("lkl_abi_version", "lkl_status_string", "lkl_workspace_size", "lkl_lse",
            "lkl_kl_forward", "lkl_forward", "lkl_backward", "lkl_device_status",
-           "lkl_last_path", "lkl_set_force_generic", "lkl_forward_noalloc")
+           "lkl_last_path", "lkl_set_force_generic", "lkl_forward_noalloc",
+           "lkl_last_cuda_error")
 
 
 class LKLProblem(ctypes.Structure):
@@ -46,6 +47,8 @@ class LKLError(RuntimeError):
     def __init__(self, status: int, where: str):
         self.status = status
         msg = _lib_handle.lkl_status_string(status).decode() if _lib_handle else ""
+        if status == 7 and _lib_handle is not None:
+            msg += f"; cudaError {_lib_handle.lkl_last_cuda_error()}"
         super().__init__(f"{where}: {STATUS.get(status, status)} ({msg})")
 
 
@@ -72,6 +75,7 @@ def _declare(L):
     L.lkl_backward.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _P, _vp, _vp, _vp, _vp, _sz, _vp]
     L.lkl_device_status.restype = _i32
     L.lkl_last_path.restype = _i32
+    L.lkl_last_cuda_error.restype = _i32
     L.lkl_set_force_generic.restype = None
     L.lkl_set_force_generic.argtypes = [_i32]
     L.lkl_forward_noalloc.restype = _i32

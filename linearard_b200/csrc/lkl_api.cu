@@ -15,6 +15,7 @@ namespace {
 using lkl::Problem;
 
 thread_local int32_t t_last_path = -1;
+thread_local int32_t t_last_cuda_error = 0;
 std::atomic<int32_t> g_force_generic{0};
 
 inline bool head_dim_ok(int d) {
@@ -26,6 +27,12 @@ inline size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 inline size_t bits_bytes(const lkl_problem* p) {
   return round256((size_t)p->B * (size_t)((p->T + 31) / 32) * sizeof(uint32_t));
 }
+
+inline size_t lsc_bytes(const lkl_problem* p) {
+  return round256((size_t)p->B * p->Hq * p->T * 2 * sizeof(float));
+}
+
+Problem to_problem(const lkl_problem* p);
 
 inline int max_partials(const Problem& q) {
   const int a = lkl::generic_num_partials(q), b = lkl::sm100_num_partials(q);
@@ -84,6 +91,20 @@ int32_t check_workspace(const lkl_problem* p, const void* mask, void* ws, size_t
   return LKL_OK;
 }
 
+// Makes the device that owns `ptr` current on this host thread (which also
+// makes its primary context current: callers such as PyTorch's autograd
+// worker threads may enter without one, and the TMA descriptor encoder needs
+// it).  Returns false if `ptr` is not device memory.
+bool bind_device_of(const void* ptr) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged) return false;
+  return cudaSetDevice(a.device) == cudaSuccess;
+}
+
 bool device_is_sm100() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
@@ -101,7 +122,10 @@ bool use_tensor_cores(const Problem& q, const void* a, const void* b, const void
   return lkl::sm100_supports(q);
 }
 
-inline int32_t launch_status(cudaError_t e) { return e == cudaSuccess ? LKL_OK : LKL_ERR_LAUNCH; }
+inline int32_t launch_status(cudaError_t e) {
+  if (e != cudaSuccess) t_last_cuda_error = (int32_t)e;
+  return e == cudaSuccess ? LKL_OK : LKL_ERR_LAUNCH;
+}
 
 // Packs the mask (if any) into the workspace; returns the bits pointer via *bits.
 int32_t prepare_mask(const lkl_problem* p, const void* mask, void* ws, uint32_t** bits,
@@ -114,6 +138,13 @@ int32_t prepare_mask(const lkl_problem* p, const void* mask, void* ws, uint32_t*
 
 inline float* partials_ptr(const lkl_problem* p, const void* mask, void* ws) {
   return reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + (mask ? bits_bytes(p) : 0));
+}
+
+// Backward scratch: per-row exponent offsets (float2) after the bits and partials.
+inline float2* lsc_ptr(const lkl_problem* p, const void* mask, void* ws) {
+  const size_t off = (mask ? bits_bytes(p) : 0) +
+                     round256((size_t)max_partials(to_problem(p)) * sizeof(float));
+  return reinterpret_cast<float2*>(static_cast<uint8_t*>(ws) + off);
 }
 
 }  // namespace
@@ -145,6 +176,7 @@ size_t lkl_workspace_size(const lkl_problem* p, int32_t has_mask) {
   const Problem q = to_problem(p);
   size_t n = round256((size_t)max_partials(q) * sizeof(float));
   if (has_mask) n += bits_bytes(p);
+  n += lsc_bytes(p);
   return n;
 }
 
@@ -157,7 +189,7 @@ int32_t lkl_lse(const void* q, const void* k, const void* mask, const lkl_proble
   if ((s = check_mask(mask, p->mask_dtype))) return s;
   if (p->B == 0 || p->T == 0) return LKL_OK;
   if ((s = check_workspace(p, mask, ws, ws_bytes))) return s;
-  if (!device_is_sm100()) return LKL_ERR_NO_DEVICE;
+  if (!bind_device_of(q) || !device_is_sm100()) return LKL_ERR_NO_DEVICE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint32_t* bits;
   if ((s = prepare_mask(p, mask, ws, &bits, st))) return s;
@@ -184,7 +216,7 @@ int32_t lkl_kl_forward(const void* qs, const void* ks, const float* lse_s, const
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (p->B == 0 || p->T == 0) return launch_status(cudaMemsetAsync(loss, 0, sizeof(float), st));
   if ((s = check_workspace(p, mask, ws, ws_bytes))) return s;
-  if (!device_is_sm100()) return LKL_ERR_NO_DEVICE;
+  if (!bind_device_of(qs) || !device_is_sm100()) return LKL_ERR_NO_DEVICE;
   uint32_t* bits;
   if ((s = prepare_mask(p, mask, ws, &bits, st))) return s;
   const Problem q = to_problem(p);
@@ -193,7 +225,7 @@ int32_t lkl_kl_forward(const void* qs, const void* ks, const float* lse_s, const
   cudaError_t e = lkl::launch_generic_forward(2, q, qs, ks, qt, kt, bits,
                                               const_cast<float*>(lse_s),
                                               const_cast<float*>(lse_t), part, &np, st);
-  if (e != cudaSuccess) return LKL_ERR_LAUNCH;
+  if (e != cudaSuccess) return launch_status(e);
   return launch_status(lkl::launch_reduce_partials(part, np, loss, st));
 }
 
@@ -210,7 +242,7 @@ int32_t lkl_forward(const void* qs, const void* ks, const void* qt, const void* 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (p->B == 0 || p->T == 0) return launch_status(cudaMemsetAsync(loss, 0, sizeof(float), st));
   if ((s = check_workspace(p, mask, ws, ws_bytes))) return s;
-  if (!device_is_sm100()) return LKL_ERR_NO_DEVICE;
+  if (!bind_device_of(qs) || !device_is_sm100()) return LKL_ERR_NO_DEVICE;
   uint32_t* bits;
   if ((s = prepare_mask(p, mask, ws, &bits, st))) return s;
   const Problem q = to_problem(p);
@@ -224,7 +256,7 @@ int32_t lkl_forward(const void* qs, const void* ks, const void* qt, const void* 
     t_last_path = 0;
     e = lkl::launch_generic_forward(1, q, qs, ks, qt, kt, bits, lse_s, lse_t, part, &np, st);
   }
-  if (e != cudaSuccess) return LKL_ERR_LAUNCH;
+  if (e != cudaSuccess) return launch_status(e);
   return launch_status(lkl::launch_reduce_partials(part, np, loss, st));
 }
 
@@ -244,19 +276,21 @@ int32_t lkl_backward(const void* qs, const void* ks, const float* lse_s, const v
   if (alias && (qs != ks || p->Hkv_s != p->Hq)) return LKL_ERR_BAD_ALIAS;
   if (p->B == 0 || p->T == 0) return LKL_OK;
   if ((s = check_workspace(p, mask, ws, ws_bytes))) return s;
-  if (!device_is_sm100()) return LKL_ERR_NO_DEVICE;
+  if (!bind_device_of(qs) || !device_is_sm100()) return LKL_ERR_NO_DEVICE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint32_t* bits;
   if ((s = prepare_mask(p, mask, ws, &bits, st))) return s;
   const Problem q = to_problem(p);
-  // dk (and dq when it is the same buffer) accumulates with vector reductions
-  const size_t dk_bytes = (size_t)p->B * p->Hkv_s * p->T * p->Ds * sizeof(float);
-  if (cudaMemsetAsync(dk, 0, dk_bytes, st) != cudaSuccess) return LKL_ERR_LAUNCH;
   cudaError_t e;
-  if (use_tensor_cores(q, qs, ks, qt, kt)) {
+  if (use_tensor_cores(q, qs, ks, qt, kt) && lkl::sm100_backward_supports(q)) {
+    // every gradient row is written by exactly one CTA: no clearing needed
     t_last_path = 1;
-    e = lkl::launch_sm100_backward(q, qs, ks, lse_s, qt, kt, lse_t, bits, dloss, dq, dk, alias, st);
+    e = lkl::launch_sm100_backward(q, qs, ks, lse_s, qt, kt, lse_t, bits, dloss, dq, dk, alias,
+                                   lsc_ptr(p, mask, ws), st);
   } else {
+    // dk (and dq when it is the same buffer) accumulates with atomics
+    const size_t dk_bytes = (size_t)p->B * p->Hkv_s * p->T * p->Ds * sizeof(float);
+    if (cudaMemsetAsync(dk, 0, dk_bytes, st) != cudaSuccess) return LKL_ERR_LAUNCH;
     t_last_path = 0;
     e = lkl::launch_generic_backward(q, qs, ks, lse_s, qt, kt, lse_t, bits, dloss, dq, dk, alias,
                                      st);
@@ -277,6 +311,8 @@ int32_t lkl_device_status(void) {
 }
 
 int32_t lkl_last_path(void) { return t_last_path; }
+
+int32_t lkl_last_cuda_error(void) { return t_last_cuda_error; }
 
 void lkl_set_force_generic(int32_t force) { g_force_generic.store(force ? 1 : 0); }
 

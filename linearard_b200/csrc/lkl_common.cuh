@@ -87,9 +87,13 @@ cudaError_t launch_sm100_forward(const Problem& p, const void* qs, const void* k
                                  const void* qt, const void* kt, const uint32_t* bits,
                                  float* lse_s, float* lse_t, float* partials,
                                  int* num_partials, cudaStream_t st);
+// Backward (dq then dk, no reductions); needs Hkv_s == Hkv_t.  `lsc` is
+// B*Hq*T float2 of scratch for the per-row exponent offsets.
+bool sm100_backward_supports(const Problem& p);
 cudaError_t launch_sm100_backward(const Problem& p, const void* qs, const void* ks,
                                   const float* lse_s, const void* qt, const void* kt,
                                   const float* lse_t, const uint32_t* bits, const float* dloss,
-                                  float* dq, float* dk, bool alias, cudaStream_t st);
+                                  float* dq, float* dk, bool alias, float2* lsc,
+                                  cudaStream_t st);
 
 }  // namespace lkl

@@ -69,6 +69,8 @@ int32_t lkl_forward_noalloc(const void* qs, const void* ks, const void* qt, cons
   if (need > kNoAllocScratchBytes) return LKL_ERR_TOO_LARGE;
   int32_t status = LKL_OK;
   void* scratch = nullptr;
+  // the scratch address is per device: look it up on the device of the inputs
+  if (need > 0 && qs && !bind_device_of(qs)) return LKL_ERR_NO_DEVICE;
   if (need > 0) {
     scratch = noalloc_scratch_for_current_device(&status);
     if (!scratch) return status;

@@ -367,6 +367,33 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs,
 }
 
 // ============================================================== backward
+// The gradient is computed by two reduction-free launches of one kernel:
+//   DK = false: row-stationary (query tile i, key tiles j <= i):
+//               dq_i = sc * sum_j D_ij Ks_j
+//   DK = true : column-stationary (key tile j, query tiles i >= j of every
+//               query head of its kv group): dk_j = sc * sum_i D_ij Qs_i
+// Both recompute the scores of their tile pairs and D = e^{ss - lse_s} -
+// e^{st - lse_t}, rounded to the input dtype (kernel_C.py:224-233).  Each
+// output row is owned by exactly one CTA and written once, so no fp32
+// partials go through L2 reductions and the gradients are reproducible bit
+// for bit (the reference adds dk with float atomics, kernel_C.py:242-253).
+// The price is computing the scores and exponentials of each tile pair twice.
+//
+// The two variants run the same MMA sequence: the stationary operand tile
+// (Q for dq, K for dk) is A of the score GEMMs, the streamed tile is B, and
+// the gradient GEMM multiplies D (or D^T) from shared memory by the streamed
+// tile's student half read as an MN-major operand.  For dk the TMEM scores
+// are transposed (lane = key j, column = query i).
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2t(float a, float b) {
+  if (BF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
 __device__ __forceinline__ uint32_t pack2(float a, float b, int bf16) {
   if (bf16) {
     __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
@@ -376,10 +403,31 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, int bf16) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Per-row exponent offsets (lse_s, lse_t) * log2(e), or +inf for rows that take
+// no gradient (padding mask, non-finite LSE): e^{s - inf} = 0 removes them
+// without a branch.
+__global__ void scale_lse_kernel(const float* __restrict__ lse_s, const float* __restrict__ lse_t,
+                                 const uint32_t* __restrict__ bits, int B, int Hq, int T,
+                                 float2* __restrict__ out) {
+  const size_t total = (size_t)B * Hq * T;
+  const int words = (T + 31) >> 5;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    const int i = (int)(idx % T);
+    const int b = (int)(idx / T) / Hq;
+    const float ls = lse_s[idx], lt = lse_t[idx];
+    const bool ok = token_valid(bits, words, b, i) && isfinite(ls) && isfinite(lt);
+    out[idx] = ok ? make_float2(ls * kLog2e, lt * kLog2e)
+                  : make_float2(CUDART_INF_F, CUDART_INF_F);
+  }
+}
+
+// DS/2 fp32 columns of this thread's TMEM lane, times `scale`, into
+// row_ptr[0 .. DS/2): stored, or added to what is there (read-modify-write by
+// the row's only owner).
 template <int DS>
-__device__ __forceinline__ void drain_rows(uint32_t taddr, float* row_ptr, float scale,
-                                           bool do_store, bool atomic) {
-  // DS/2 fp32 columns of this thread's TMEM lane -> row_ptr[0 .. DS/2)
+__device__ __forceinline__ void store_rows(uint32_t taddr, float* row_ptr, float scale,
+                                           bool do_store, bool accumulate) {
 #pragma unroll
   for (int c = 0; c < DS / 2; c += 32) {
     float v[32];
@@ -388,52 +436,64 @@ __device__ __forceinline__ void drain_rows(uint32_t taddr, float* row_ptr, float
     if (do_store) {
 #pragma unroll
       for (int k = 0; k < 32; k += 4) {
-        float4 f = make_float4(v[k] * scale, v[k + 1] * scale, v[k + 2] * scale, v[k + 3] * scale);
         float4* dst = reinterpret_cast<float4*>(row_ptr + c + k);
-        if (atomic) atomicAdd(dst, f);
-        else *dst = f;
+        float4 f = make_float4(v[k] * scale, v[k + 1] * scale, v[k + 2] * scale, v[k + 3] * scale);
+        if (accumulate) {
+          const float4 o = *dst;
+          f.x += o.x;
+          f.y += o.y;
+          f.z += o.z;
+          f.w += o.w;
+        }
+        *dst = f;
       }
     }
   }
 }
 
-// dk_part^T (TMEM lane = feature d, column = key row j) -> dk[j][d]: the 32
-// lanes of a warp are 32 consecutive features of one key row, so every
-// reduction instruction of the warp covers 128 contiguous bytes.
-__device__ __forceinline__ void drain_dkT(uint32_t taddr, float* dk_head, int j0, int d, int T,
-                                          int DS, float scale) {
-#pragma unroll
-  for (int c = 0; c < 64; c += 32) {
-    float v[32];
-    tmem_ld32(taddr + c, v);
-    tmem_wait_ld();
-#pragma unroll
-    for (int k = 0; k < 32; ++k) {
-      const int j = j0 + c + k;
-      if (j < T) atomicAdd(dk_head + (size_t)j * DS + d, v[k] * scale);
-    }
-  }
-}
-
-template <int DS, int DT>
+template <int DS, int DT, bool DK, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
-sm100_backward_kernel(const __grid_constant__ CUtensorMap tm_qs,
-                      const __grid_constant__ CUtensorMap tm_ks,
-                      const __grid_constant__ CUtensorMap tm_qt,
-                      const __grid_constant__ CUtensorMap tm_kt, const Problem p,
-                      const float* __restrict__ lse_s, const float* __restrict__ lse_t,
-                      const uint32_t* __restrict__ bits, const float* __restrict__ dloss,
-                      float* dq, float* dk, int alias) {
-  using L = BwdLayout<DS, DT>;
+sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
+                  const __grid_constant__ CUtensorMap tm_ks,
+                  const __grid_constant__ CUtensorMap tm_qt,
+                  const __grid_constant__ CUtensorMap tm_kt, const Problem p,
+                  const float2* __restrict__ lsc, const uint32_t* __restrict__ bits,
+                  const float* __restrict__ dloss, float* out, int accumulate) {
+  using L = BwdLayout<DS, DT>;  // stationary tiles at OFF_QS / OFF_QT, streamed in stages
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   Misc* misc = reinterpret_cast<Misc*>(smem + L::OFF_MISC);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const Tile t = tile_of(p);
   int* err = &g_device_error;
   volatile int* abort = &misc->abort;
-  constexpr uint32_t kColDq = 256, kColDk = 256 + DS;
-  constexpr bool kDkT = DS == 128;
+  constexpr uint32_t kColAcc = 256;
+
+  // ---- work of this CTA (head-major, longest first)
+  const int n_t = (p.T + kBM - 1) / kBM;
+  int b, hs, ht, st_tile, n_steps, n_per_head, first_tile, bh0;
+  if (DK) {
+    const int G = p.Hq / p.Hkv_s;
+    const int bk = (int)(blockIdx.x / n_t);
+    st_tile = (int)(blockIdx.x % n_t);  // key tile, ascending = longest first
+    b = bk / p.Hkv_s;
+    hs = bk % p.Hkv_s;
+    ht = hs;  // the tensor-core dk path requires Hkv_s == Hkv_t
+    first_tile = p.causal ? st_tile : 0;
+    n_per_head = n_t - first_tile;
+    n_steps = G * n_per_head;
+    bh0 = b * p.Hq + hs * G;
+  } else {
+    const int bh = (int)(blockIdx.x / n_t);
+    st_tile = n_t - 1 - (int)(blockIdx.x % n_t);  // query tile, descending = longest first
+    b = bh / p.Hq;
+    const int h = bh % p.Hq;
+    hs = h / (p.Hq / p.Hkv_s);
+    ht = h / (p.Hq / p.Hkv_t);
+    first_tile = 0;
+    n_per_head = p.causal ? st_tile + 1 : n_t;
+    n_steps = n_per_head;
+    bh0 = bh;
+  }
 
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_qs);
@@ -446,27 +506,38 @@ sm100_backward_kernel(const __grid_constant__ CUtensorMap tm_qs,
 
   if (warp == 0) {
     if (lane == 0) {
+      // ---------------- TMA producer
       mbar_arrive_expect_tx(&misc->q_full, L::QS + L::QT);
-      issue_tile_loads(smem + L::OFF_QS, &tm_qs, &misc->q_full, DS, t.mt * kBM, t.bh);
-      issue_tile_loads(smem + L::OFF_QT, &tm_qt, &misc->q_full, DT, t.mt * kBM, t.bh);
-      const int zs = t.b * p.Hkv_s + t.hs, zt = t.b * p.Hkv_t + t.ht;
-      for (int j = 0; j < t.n_ct; ++j) {
+      if (DK) {
+        issue_tile_loads(smem + L::OFF_QS, &tm_ks, &misc->q_full, DS, st_tile * kBM, b * p.Hkv_s + hs);
+        issue_tile_loads(smem + L::OFF_QT, &tm_kt, &misc->q_full, DT, st_tile * kBM, b * p.Hkv_t + ht);
+      } else {
+        issue_tile_loads(smem + L::OFF_QS, &tm_qs, &misc->q_full, DS, st_tile * kBM, bh0);
+        issue_tile_loads(smem + L::OFF_QT, &tm_qt, &misc->q_full, DT, st_tile * kBM, bh0);
+      }
+      for (int j = 0; j < n_steps; ++j) {
         const int s = j % L::NS;
         if (j >= L::NS && !mbar_wait(&misc->k_empty[s], ((j / L::NS) - 1) & 1, abort, err)) break;
-        uint8_t* st = smem + L::OFF_K + s * L::STAGE;
+        uint8_t* stg = smem + L::OFF_K + s * L::STAGE;
         mbar_arrive_expect_tx(&misc->k_full[s], L::STAGE);
-        issue_tile_loads(st, &tm_ks, &misc->k_full[s], DS, j * kBN, zs);
-        issue_tile_loads(st + kBN * DS * 2, &tm_kt, &misc->k_full[s], DT, j * kBN, zt);
+        const int tile = first_tile + j % n_per_head;
+        if (DK) {
+          const int bh = bh0 + j / n_per_head;
+          issue_tile_loads(stg, &tm_qs, &misc->k_full[s], DS, tile * kBN, bh);
+          issue_tile_loads(stg + kBN * DS * 2, &tm_qt, &misc->k_full[s], DT, tile * kBN, bh);
+        } else {
+          issue_tile_loads(stg, &tm_ks, &misc->k_full[s], DS, tile * kBN, b * p.Hkv_s + hs);
+          issue_tile_loads(stg + kBN * DS * 2, &tm_kt, &misc->k_full[s], DT, tile * kBN,
+                           b * p.Hkv_t + ht);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      // ---------------- MMA issuer: scores of step j+1 ahead of the gradient GEMM of j
       const uint32_t id_s = idesc_f16(kBM, kBN, p.dtype_s, p.dtype_s, 0, 0);
       const uint32_t id_t = idesc_f16(kBM, kBN, p.dtype_t, p.dtype_t, 0, 0);
-      const uint32_t id_dq = idesc_f16(kBM, DS, p.dtype_s, p.dtype_s, 0, 1);
-      // DS == 128: dk_part^T = Qs^T D (M = d, N = j); otherwise dk_part = D^T Qs
-      const uint32_t id_dk = kDkT ? idesc_f16(DS, kBN, p.dtype_s, p.dtype_s, 1, 1)
-                                  : idesc_f16(kBN, DS, p.dtype_s, p.dtype_s, 1, 1);
+      const uint32_t id_g = idesc_f16(kBM, DS, p.dtype_s, p.dtype_s, 0, 1);
       const uint32_t a_s = smem_u32(smem + L::OFF_QS), a_t = smem_u32(smem + L::OFF_QT);
       const uint32_t a_d = smem_u32(smem + L::OFF_DEL);
       auto issue_scores = [&](int j) {
@@ -487,8 +558,8 @@ sm100_backward_kernel(const __grid_constant__ CUtensorMap tm_qs,
         tc_fence_after();
         issue_scores(0);
       }
-      for (int j = 0; ok && j < t.n_ct; ++j) {
-        if (j + 1 < t.n_ct) {
+      for (int j = 0; ok && j < n_steps; ++j) {
+        if (j + 1 < n_steps) {
           const int s1 = (j + 1) % L::NS;
           if (!mbar_wait(&misc->k_full[s1], ((j + 1) / L::NS) & 1, abort, err)) break;
           if (!mbar_wait(&misc->s_empty[0], j & 1, abort, err)) break;
@@ -499,95 +570,112 @@ sm100_backward_kernel(const __grid_constant__ CUtensorMap tm_qs,
         tc_fence_after();
         const int s = j % L::NS;
         const uint32_t b_s = smem_u32(smem + L::OFF_K + s * L::STAGE);
-        // dq(i, :) += D(i, j) Ks(j, :)     A = D K-major, B = Ks MN-major
+        // acc += D . X  with D K-major and X = the streamed student tile, MN-major
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk)
-          umma_f16_ss(tmem + kColDq, kmajor_desc(a_d, kk), mnmajor_desc(b_s, kk), id_dq,
+          umma_f16_ss(tmem + kColAcc, kmajor_desc(a_d, kk), mnmajor_desc(b_s, kk), id_g,
                       (j > 0 || kk > 0) ? 1u : 0u);
-        if (kDkT) {
-          // dk_part^T(:, j) = Qs(i, :)^T D(i, j)  A = Qs MN-major, B = D MN-major
-#pragma unroll
-          for (int kk = 0; kk < kBM / 16; ++kk)
-            umma_f16_ss(tmem + kColDk, mnmajor_desc(a_s, kk), mnmajor_desc(a_d, kk), id_dk,
-                        kk > 0 ? 1u : 0u);
-        } else {
-          // dk_part(j, :) = D(i, j)^T Qs(i, :)  A = D MN-major, B = Qs MN-major
-#pragma unroll
-          for (int kk = 0; kk < kBM / 16; ++kk)
-            umma_f16_ss(tmem + kColDk, mnmajor_desc(a_d, kk), mnmajor_desc(a_s, kk), id_dk,
-                        kk > 0 ? 1u : 0u);
-        }
         umma_commit(&misc->d_empty);
         umma_commit(&misc->k_empty[s]);
       }
     }
   } else if (warp >= 4) {
+    // ---------------- row warps: lane r of the stationary tile, 64 streamed
+    // columns (of each 128) per warpgroup
     const int wg = (warp - 4) >> 2, q = warp & 3;
     const int r = q * 32 + lane;
-    const int i = t.mt * kBM + r;
     const int words = (p.T + 31) >> 5;
-    const bool row_in = i < p.T;
-    float Ls = 0.f, Lt = 0.f;
-    bool row_ok = row_in && token_valid(bits, words, t.b, i);
-    if (row_in) {
-      Ls = lse_s[(size_t)t.bh * p.T + i];
-      Lt = lse_t[(size_t)t.bh * p.T + i];
-      row_ok = row_ok && isfinite(Ls) && isfinite(Lt);
-    }
-    const float Ls2 = Ls * kLog2e, Lt2 = Lt * kLog2e;
-    const int lim = p.causal ? min(i, p.T - 1) : p.T - 1;
+    const int own = st_tile * kBM + r;  // query row (dq) or key row (dk) of this lane
+    const bool own_in = own < p.T;
     const float cs = p.sc_s * kLog2e, ct = p.sc_t * kLog2e;
     const float gscale = p.sc_s * (dloss ? *dloss : 1.f);
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
     uint8_t* del_row = smem + L::OFF_DEL + wg * kChunk + r * 128;
-    const int bf16 = p.dtype_s == LKL_BF16;
-    float* dk_head = dk + ((size_t)t.b * p.Hkv_s + t.hs) * (size_t)p.T * DS;
+    // dq: this row's exponent offsets; dk: whether this key takes part at all
+    float2 Lrow = make_float2(CUDART_INF_F, CUDART_INF_F);
+    bool key_ok = true;
+    if (!DK) {
+      if (own_in) Lrow = lsc[(size_t)bh0 * p.T + own];
+    } else {
+      key_ok = own_in && token_valid(bits, words, b, own);
+    }
+    const bool row_live = DK ? key_ok : (Lrow.x != CUDART_INF_F);
 
-    for (int j = 0; j < t.n_ct; ++j) {
+    for (int j = 0; j < n_steps; ++j) {
+      const int tile = first_tile + j % n_per_head;
+      // dk: lane k fetches the exponent offsets of columns k and 32 + k of this
+      // warpgroup's 64 query rows before the scores arrive; they are handed to
+      // the other lanes with shuffles
+      float2 lA = make_float2(0.f, 0.f), lB = make_float2(0.f, 0.f);
+      if (DK) {
+        const float2* lcol = lsc + (size_t)(bh0 + j / n_per_head) * p.T;
+        const int cb = tile * kBN + wg * 64 + lane;
+        lA = lcol[min(cb, p.T - 1)];
+        lB = lcol[min(cb + 32, p.T - 1)];
+      }
       if (!mbar_wait(&misc->s_full[0], j & 1, abort, err)) break;
       tc_fence_after();
       uint32_t packed[32];
+      // load all 64 ss and 64 st values of this thread first and release the
+      // (single) score buffer at once, so the next tile's score GEMMs run
+      // under this tile's exponentials
+      float xa[2][32], ya[2][32];
+      tmem_ld32(lane_addr + wg * 64, xa[0]);
+      tmem_ld32(lane_addr + 128 + wg * 64, ya[0]);
+      tmem_ld32(lane_addr + wg * 64 + 32, xa[1]);
+      tmem_ld32(lane_addr + 128 + wg * 64 + 32, ya[1]);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&misc->s_empty[0]);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
-        float x[32], y[32];
-        const uint32_t col = wg * 64 + half * 32;
-        tmem_ld32(lane_addr + col, x);
-        tmem_ld32(lane_addr + 128 + col, y);
-        tmem_wait_ld();
-        if (half == 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&misc->s_empty[0]);
-        }
-        const int c0 = j * kBN + wg * 64 + half * 32;
-        const bool full = row_ok && (c0 + 31 <= lim) && (bits == nullptr);
+        float(&x)[32] = xa[half];
+        float(&y)[32] = ya[half];
+        const int c0 = tile * kBN + wg * 64 + half * 32;  // first streamed row of these columns
+        // (no early exit for dead rows: the dk branch shuffles across the warp)
+        float d[32];
+        bool full;
+        if (!DK) {
 #pragma unroll
-        for (int k = 0; k < 32; k += 2) {
-          float d0 = ex2(fmaf(x[k], cs, -Ls2)) - ex2(fmaf(y[k], ct, -Lt2));
-          float d1 = ex2(fmaf(x[k + 1], cs, -Ls2)) - ex2(fmaf(y[k + 1], ct, -Lt2));
+          for (int k = 0; k < 32; ++k)
+            d[k] = ex2(fmaf(x[k], cs, -Lrow.x)) - ex2(fmaf(y[k], ct, -Lrow.y));
+          // columns are keys c: valid iff c <= i (causal), c < T, key not padded
+          const int lim = p.causal ? min(own, p.T - 1) : p.T - 1;
+          full = (c0 + 31 <= lim) && (bits == nullptr);
           if (!full) {
-            const int c = c0 + k;
-            const bool ok0 = row_ok && (c <= lim) && token_valid(bits, words, t.b, c);
-            const bool ok1 = row_ok && (c + 1 <= lim) && token_valid(bits, words, t.b, c + 1);
-            d0 = ok0 ? d0 : 0.f;
-            d1 = ok1 ? d1 : 0.f;
+#pragma unroll
+            for (int k = 0; k < 32; ++k)
+              if (!((c0 + k <= lim) && token_valid(bits, words, b, c0 + k))) d[k] = 0.f;
           }
-          packed[half * 16 + (k >> 1)] = pack2(d0, d1, bf16);
+        } else {
+          const float2 lh = half ? lB : lA;
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            const float lx = __shfl_sync(0xffffffffu, lh.x, k);
+            const float ly = __shfl_sync(0xffffffffu, lh.y, k);
+            d[k] = ex2(fmaf(x[k], cs, -lx)) - ex2(fmaf(y[k], ct, -ly));
+          }
+          // columns are query rows c: valid iff c >= j (causal) and c < T; padded
+          // or LSE-less rows carry +inf offsets and give 0 by themselves
+          full = (!p.causal || c0 >= own) && (c0 + 31 < p.T);
+          if (!full) {
+#pragma unroll
+            for (int k = 0; k < 32; ++k)
+              if (!((c0 + k < p.T) && (!p.causal || c0 + k >= own))) d[k] = 0.f;
+          }
         }
+        if (!row_live) {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) d[k] = 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < 32; k += 2) packed[half * 16 + (k >> 1)] = pack2t<BF16>(d[k], d[k + 1]);
       }
       if (j > 0) {
         if (!mbar_wait(&misc->d_empty, (j - 1) & 1, abort, err)) break;
-        tc_fence_after();
-        if (kDkT) {
-          drain_dkT(lane_addr + kColDk + wg * 64, dk_head, (j - 1) * kBN + wg * 64, r, p.T, DS,
-                    gscale);
-        } else {
-          const int jr = (j - 1) * kBN + r;
-          drain_rows<DS>(lane_addr + kColDk + wg * (DS / 2),
-                         dk_head + (size_t)jr * DS + wg * (DS / 2), gscale, jr < p.T, true);
-        }
       }
-      // D row r, 64 columns of chunk wg: 8 x 16 B pieces, 128B-swizzled
+      // D row r (64 columns of chunk wg): 8 x 16 B pieces, 128B-swizzled
 #pragma unroll
       for (int pc = 0; pc < 8; ++pc) {
         uint4 v = make_uint4(packed[pc * 4], packed[pc * 4 + 1], packed[pc * 4 + 2],
@@ -595,22 +683,15 @@ sm100_backward_kernel(const __grid_constant__ CUtensorMap tm_qs,
         *reinterpret_cast<uint4*>(del_row + ((pc ^ (r & 7)) << 4)) = v;
       }
       fence_proxy_async_smem();
-      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&misc->d_full);
     }
-    if (t.n_ct > 0 && mbar_wait(&misc->d_empty, (t.n_ct - 1) & 1, abort, err)) {
+    if (n_steps > 0 && mbar_wait(&misc->d_empty, (n_steps - 1) & 1, abort, err)) {
       tc_fence_after();
-      if (kDkT) {
-        drain_dkT(lane_addr + kColDk + wg * 64, dk_head, (t.n_ct - 1) * kBN + wg * 64, r, p.T,
-                  DS, gscale);
-      } else {
-        const int jr = (t.n_ct - 1) * kBN + r;
-        drain_rows<DS>(lane_addr + kColDk + wg * (DS / 2),
-                       dk_head + (size_t)jr * DS + wg * (DS / 2), gscale, jr < p.T, true);
-      }
-      float* dq_row = dq + ((size_t)t.bh * p.T + i) * DS + wg * (DS / 2);
-      drain_rows<DS>(lane_addr + kColDq + wg * (DS / 2), dq_row, gscale, row_in, alias != 0);
+      float* row = DK ? out + (((size_t)b * p.Hkv_s + hs) * p.T + own) * DS
+                      : out + ((size_t)bh0 * p.T + own) * DS;
+      store_rows<DS>(lane_addr + kColAcc + wg * (DS / 2), row + wg * (DS / 2), gscale, own_in,
+                     DK && accumulate != 0);
     }
   }
 
@@ -688,16 +769,22 @@ cudaError_t run_forward(const Problem& p, const Maps& m, const uint32_t* bits, f
 }
 
 template <int DS, int DT>
-cudaError_t run_backward(const Problem& p, const Maps& m, const float* lse_s, const float* lse_t,
-                         const uint32_t* bits, const float* dloss, float* dq, float* dk,
-                         bool alias, cudaStream_t st) {
+cudaError_t run_grad(const Problem& p, const Maps& m, const float2* lsc, const uint32_t* bits,
+                     const float* dloss, float* dq, float* dk, bool alias, cudaStream_t st) {
   using L = BwdLayout<DS, DT>;
-  auto k = sm100_backward_kernel<DS, DT>;
-  cudaError_t e = prep(k, L::BYTES);
+  const bool bf = p.dtype_s == LKL_BF16;
+  auto kq = bf ? sm100_grad_kernel<DS, DT, false, true> : sm100_grad_kernel<DS, DT, false, false>;
+  auto kk = bf ? sm100_grad_kernel<DS, DT, true, true> : sm100_grad_kernel<DS, DT, true, false>;
+  cudaError_t e = prep(kq, L::BYTES);
+  if (e == cudaSuccess) e = prep(kk, L::BYTES);
   if (e != cudaSuccess) return e;
-  const int grid = sm100_num_partials(p);
-  k<<<grid, kThreads, L::BYTES, st>>>(m.qs, m.ks, m.qt, m.kt, p, lse_s, lse_t, bits, dloss, dq,
-                                       dk, alias ? 1 : 0);
+  const int n_t = (p.T + kBM - 1) / kBM;
+  // dq first (plain stores); then dk, which in the fused case adds into the same rows
+  kq<<<p.B * p.Hq * n_t, kThreads, L::BYTES, st>>>(m.qs, m.ks, m.qt, m.kt, p, lsc, bits, dloss,
+                                                    dq, 0);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  kk<<<p.B * p.Hkv_s * n_t, kThreads, L::BYTES, st>>>(m.qs, m.ks, m.qt, m.kt, p, lsc, bits,
+                                                       dloss, alias ? dq : dk, alias ? 1 : 0);
   return cudaGetLastError();
 }
 
@@ -724,19 +811,26 @@ cudaError_t launch_sm100_forward(const Problem& p, const void* qs, const void* k
   return run_forward<64, 128>(p, m, bits, lse_s, lse_t, partials, st);
 }
 
+bool sm100_backward_supports(const Problem& p) {
+  return sm100_supports(p) && p.Hkv_s == p.Hkv_t;
+}
+
 cudaError_t launch_sm100_backward(const Problem& p, const void* qs, const void* ks,
                                   const float* lse_s, const void* qt, const void* kt,
                                   const float* lse_t, const uint32_t* bits, const float* dloss,
-                                  float* dq, float* dk, bool alias, cudaStream_t st) {
+                                  float* dq, float* dk, bool alias, float2* lsc,
+                                  cudaStream_t st) {
   Maps m;
   if (!build_maps(m, p, qs, ks, qt, kt)) return cudaErrorInvalidValue;
-  if (p.Ds == 128 && p.Dt == 128)
-    return run_backward<128, 128>(p, m, lse_s, lse_t, bits, dloss, dq, dk, alias, st);
-  if (p.Ds == 64 && p.Dt == 64)
-    return run_backward<64, 64>(p, m, lse_s, lse_t, bits, dloss, dq, dk, alias, st);
-  if (p.Ds == 128 && p.Dt == 64)
-    return run_backward<128, 64>(p, m, lse_s, lse_t, bits, dloss, dq, dk, alias, st);
-  return run_backward<64, 128>(p, m, lse_s, lse_t, bits, dloss, dq, dk, alias, st);
+  const size_t rows = (size_t)p.B * p.Hq * p.T;
+  const int grid = (int)((rows + 255) / 256 < 4096 ? (rows + 255) / 256 : 4096);
+  scale_lse_kernel<<<grid, 256, 0, st>>>(lse_s, lse_t, bits, p.B, p.Hq, p.T, lsc);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  if (p.Ds == 128 && p.Dt == 128) return run_grad<128, 128>(p, m, lsc, bits, dloss, dq, dk, alias, st);
+  if (p.Ds == 64 && p.Dt == 64) return run_grad<64, 64>(p, m, lsc, bits, dloss, dq, dk, alias, st);
+  if (p.Ds == 128 && p.Dt == 64) return run_grad<128, 64>(p, m, lsc, bits, dloss, dq, dk, alias, st);
+  return run_grad<64, 128>(p, m, lsc, bits, dloss, dq, dk, alias, st);
 }
 
 }  // namespace lkl

@@ -137,3 +137,31 @@ def test_llama3_32k_one_head_vs_oracle_slice():
     np.testing.assert_allclose(ls[:, :, :n].cpu().numpy(), rls, rtol=1e-4, atol=1e-4)
     np.testing.assert_allclose(lt[:, :, :n].cpu().numpy(), rlt, rtol=1e-4, atol=1e-4)
     assert np.isfinite(float(loss)) and float(loss) > 0
+
+
+def test_backward_from_a_fresh_host_thread():
+    """PyTorch runs backward on its own worker thread, which may have no
+    current CUDA context; every entry point binds the device of its inputs
+    itself (the tensor-map encoder needs a current context)."""
+    import threading
+    from linearard_b200.attention_KL import attn_kl_forward, kl_backward
+    s = _rand((1, 4, 300, 128), 31).cuda()
+    t = _rand((1, 4, 300, 128), 32).cuda()
+    loss, ls, lt = attn_kl_forward(s, s, t, t)
+    ref, _ = kl_backward(s, s, ls, t, t, lt, fused=True)
+    out = {}
+
+    def worker():
+        try:
+            out["dS"], _ = kl_backward(s, s, ls, t, t, lt, fused=True)
+            out["path"] = path_is_tensor_core()
+            torch.cuda.synchronize()
+        except Exception as e:  # noqa: BLE001
+            out["err"] = e
+
+    th = threading.Thread(target=worker)
+    th.start()
+    th.join()
+    assert "err" not in out, out.get("err")
+    assert out["path"]
+    torch.testing.assert_close(out["dS"], ref, rtol=0, atol=0)
