@@ -3,8 +3,8 @@
 // Both kernels are row-stationary: one CTA owns a 128-row tile i of one
 // (batch, query head) and walks the 128-column tiles j <= i (all j when not
 // causal).  Operand tiles are staged by TMA (128-byte swizzle, no multicast),
-// scores are computed by tcgen05.mma into TMEM, and eight "row" warps (two
-// warpgroups, each owning 64 of the 128 columns of a tile for all 128 rows)
+// scores are computed by tcgen05.mma into TMEM, and sixteen "row" warps (four
+// warpgroups, each owning 32 of the 128 columns of a tile for all 128 rows)
 // read them back with tcgen05.ld.
 //
 // Forward (replaces kernel_A x2 + kernel_B, kernel_A.py:42-159 / kernel_B.py:57-218):
@@ -21,9 +21,9 @@
 //   transpose Qs_i^T D, so that TMEM lanes are features), the latter drained
 //   by the row warps with fp32 reductions into dk.
 //
-// Warp roles (384 threads): warp 0 = TMA producer, warp 1 = MMA issuer and
-// TMEM owner, warps 2-3 idle, warps 4-11 = row warps (warp w reads TMEM
-// lanes 32*(w%4) .. +31).
+// Warp roles (576 threads): warps 0-15 = row warps in four warpgroups (warp
+// w reads TMEM lanes 32*(w%4) .. +31; warpgroup g owns 32 of each tile's 128
+// columns), warp 16 = TMA producer, warp 17 = MMA issuer and TMEM owner.
 #include <math_constants.h>
 
 #include <mutex>
@@ -39,7 +39,13 @@ using namespace sm100;
 constexpr int kBM = 128;          // rows per tile (= TMEM lanes)
 constexpr int kBN = 128;          // columns per tile
 constexpr int kChunk = 128 * 64 * 2;  // one [128 rows][64 elems] 16-bit swizzled chunk
-constexpr int kThreads = 384;
+// Warp roles: warps 0-15 = four row warpgroups (warp w reads TMEM lanes
+// 32*(w%4) and owns 32 of each tile's 128 columns), warp 16 = TMA producer,
+// warp 17 = MMA issuer and TMEM owner.
+constexpr int kRowWarps = 16;
+constexpr int kProducerWarp = 16;
+constexpr int kMmaWarp = 17;
+constexpr int kThreads = 32 * (kRowWarps + 2);
 constexpr int kMaxDynSmem = 232448;
 constexpr int kMisc = 1024;
 constexpr uint32_t kTmemCols = 512;
@@ -49,6 +55,47 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// 2^x on the FMA pipe, for part of the exponentials (the MUFU unit that
+// serves ex2.approx delivers 16 results per clock per SM and is the shared
+// bound of every kernel here).  Cody-Waite style reduction: x = j + f with j
+// the nearest integer (added into the exponent bits) and f in [-1/2, 1/2],
+// then 2^f by a polynomial fitted here for minimum relative error on that
+// interval (Remez exchange in double precision):
+//   degree 3: max relative error 7.5e-5 (fp32 Horner); degree 4: 2.7e-6.
+// Inputs below -125 are clamped (result ~2e-38 instead of 0); callers use it
+// only where the argument is <= 0 and finite, or where tiny results are
+// harmless.
+template <int DEG>
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -125.0f);
+  const float t = __fadd_rn(x, 12582912.0f);  // 1.5 * 2^23: round to nearest integer
+  const float j = __fadd_rn(t, -12582912.0f);
+  const float f = __fadd_rn(x, -j);
+  float p;
+  if (DEG == 3) {
+    p = fmaf(5.517166907e-02f, f, 2.426111222e-01f);
+    p = fmaf(p, f, 6.932609855e-01f);
+    p = fmaf(p, f, 9.999280735e-01f);
+  } else {
+    p = fmaf(9.570101908e-03f, f, 5.591786032e-02f);
+    p = fmaf(p, f, 2.402474483e-01f);
+    p = fmaf(p, f, 6.931218147e-01f);
+    p = fmaf(p, f, 9.999992614e-01f);
+  }
+  const int ji = __float_as_int(t) - 0x4B400000;
+  return __int_as_float(__float_as_int(p) + (ji << 23));
+}
+
+// Exponentials of element k of a 32-element chunk: every kPolyEvery-th one on
+// the FMA pipe (0 = none).
+template <int EVERY, int DEG>
+__device__ __forceinline__ float ex2_mix(float x, int k) {
+  if (EVERY > 0 && (k % EVERY) == EVERY - 1) return ex2_poly<DEG>(x);
+  return ex2(x);
+}
+constexpr int kPolyEveryFwd = 0;
+constexpr int kPolyEveryBwd = 0;
+
 __device__ __forceinline__ float lg2(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -67,7 +114,7 @@ template <int DS, int DT>
 struct FwdLayout {
   static constexpr int QS = kBM * DS * 2, QT = kBM * DT * 2;
   static constexpr int STAGE = kBN * (DS + DT) * 2;
-  static constexpr int STAT = 5 * kBM * 4;  // second warpgroup's row statistics
+  static constexpr int STAT = 3 * 5 * kBM * 4;  // row statistics of warpgroups 1-3
   static constexpr int AVAIL = kMaxDynSmem - 1024 - kMisc - STAT - QS - QT;
   static constexpr int NS = (AVAIL / STAGE) >= 4 ? 4 : (AVAIL / STAGE);
   static constexpr int OFF_QS = 0, OFF_QT = QS, OFF_K = QS + QT;
@@ -152,14 +199,14 @@ __device__ __forceinline__ void setup_cta(Misc* misc, int warp, int lane) {
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&misc->s_full[s], 1);
-      mbar_init(&misc->s_empty[s], 8);
+      mbar_init(&misc->s_empty[s], kRowWarps);
     }
-    mbar_init(&misc->d_full, 8);
+    mbar_init(&misc->d_full, kRowWarps);
     mbar_init(&misc->d_empty, 1);
     misc->abort = 0;
     fence_barrier_init();
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tmem_alloc(&misc->tmem_base, kTmemCols);
     tmem_relinquish();
   }
@@ -181,13 +228,13 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs,
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   Misc* misc = reinterpret_cast<Misc*>(smem + L::OFF_MISC);
-  float(*stat)[kBM] = reinterpret_cast<float(*)[kBM]>(smem + L::OFF_STAT);
+  float* stat = reinterpret_cast<float*>(smem + L::OFF_STAT);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Tile t = tile_of(p);
   int* err = &g_device_error;
   volatile int* abort = &misc->abort;
 
-  if (warp == 0 && lane == 0) {
+  if (warp == kProducerWarp && lane == 0) {
     tma_prefetch_desc(&tm_qs);
     tma_prefetch_desc(&tm_ks);
     tma_prefetch_desc(&tm_qt);
@@ -196,7 +243,7 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs,
   setup_cta<L>(misc, warp, lane);
   const uint32_t tmem = misc->tmem_base;
 
-  if (warp == 0) {
+  if (warp == kProducerWarp) {
     if (lane == 0) {
       // ---------------- TMA producer
       mbar_arrive_expect_tx(&misc->q_full, L::QS + L::QT);
@@ -212,7 +259,7 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs,
         issue_tile_loads(st + kBN * DS * 2, &tm_kt, &misc->k_full[s], DT, j * kBN, zt);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     if (lane == 0) {
       // ---------------- MMA issuer
       const uint32_t id_s = idesc_f16(kBM, kBN, p.dtype_s, p.dtype_s, 0, 0);
@@ -238,9 +285,9 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs,
         }
       }
     }
-  } else if (warp >= 4) {
-    // ---------------- row warps
-    const int wg = (warp - 4) >> 2, q = warp & 3;
+  } else if (warp < kRowWarps) {
+    // ---------------- row warps: warpgroup wg owns columns [32 wg, 32 wg + 32) of each tile
+    const int wg = warp >> 2, q = warp & 3;
     const int r = q * 32 + lane;
     const int i = t.mt * kBM + r;
     const int words = (p.T + 31) >> 5;
@@ -248,7 +295,7 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs,
     const bool row_valid = row_in && token_valid(bits, words, t.b, i);
     const int lim = p.causal ? min(i, p.T - 1) : p.T - 1;
     const float cs = p.sc_s * kLog2e, ct = p.sc_t * kLog2e;
-    float m_s = -CUDART_INF_F, l_s = 0.f, m_t = -CUDART_INF_F, l_t = 0.f, acc = 0.f;
+    float m_s = -CUDART_INF_F, l_s = 0.f, m_t = -CUDART_INF_F, l_t = 0.f, ay = 0.f, ax = 0.f;
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
 
     for (int j = 0; j < t.n_ct; ++j) {
@@ -256,89 +303,126 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs,
       if (!mbar_wait(&misc->s_full[bf], (j >> 1) & 1, abort, err)) break;
       tc_fence_after();
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
+      for (int chunk = 0; chunk < 1; ++chunk) {
         float x[32], y[32];
-        const uint32_t col = bf * 256 + wg * 64 + half * 32;
+        const uint32_t col = bf * 256 + wg * 32;
         tmem_ld32(lane_addr + col, x);
         tmem_ld32(lane_addr + col + 128, y);
         tmem_wait_ld();
-        if (half == 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&misc->s_empty[bf]);
-        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&misc->s_empty[bf]);
         if (!row_valid) continue;
-        const int c0 = j * kBN + wg * 64 + half * 32;
+        const int c0 = j * kBN + wg * 32;
         const bool full = (c0 + 31 <= lim) && (bits == nullptr);
         if (!full) {
-          // mask invalid columns: ss, st -> -inf, and keep the difference finite
+          // masked columns get a large finite negative score: e^(s - m) = 0 and
+          // every product below stays finite
 #pragma unroll
           for (int k = 0; k < 32; ++k) {
             const int c = c0 + k;
             const bool ok = (c <= lim) && token_valid(bits, words, t.b, c);
             if (!ok) {
-              x[k] = -CUDART_INF_F;
-              y[k] = -CUDART_INF_F;
+              x[k] = -1.0e30f;
+              y[k] = -1.0e30f;
             }
           }
         }
-        float mx = -CUDART_INF_F, my = -CUDART_INF_F;
+        float mx = x[0], my = y[0];
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          mx = fmaxf(mx, x[k]);
-          my = fmaxf(my, y[k]);
+        for (int k = 1; k < 31; k += 2) {
+          mx = fmax3(mx, x[k], x[k + 1]);
+          my = fmax3(my, y[k], y[k + 1]);
         }
-        if (my == -CUDART_INF_F) continue;  // no valid column in this chunk
+        mx = fmaxf(mx, x[31]);
+        my = fmaxf(my, y[31]);
+        if (my < -1.0e29f) continue;  // no valid column in this chunk
         const float ms_new = fmaxf(m_s, mx * cs);
         const float mt_new = fmaxf(m_t, my * ct);
         l_s *= ex2(m_s - ms_new);
         const float beta = ex2(m_t - mt_new);
         l_t *= beta;
-        acc *= beta;
-        float ls0 = 0.f, ls1 = 0.f, lt0 = 0.f, lt1 = 0.f, a0 = 0.f, a1 = 0.f;
+        ay *= beta;
+        ax *= beta;
+        // packed pairs: l_s += e^(ss - m_s); l_t += e^(st - m_t);
+        // ay += e^(st - m_t) * st_raw; ax += e^(st - m_t) * ss_raw
+        const uint64_t cs2 = f2pack(cs, cs), ct2 = f2pack(ct, ct);
+        const uint64_t nms2 = f2pack(-ms_new, -ms_new), nmt2 = f2pack(-mt_new, -mt_new);
+        uint64_t ls2 = 0, lt2 = 0, ay2 = 0, ax2 = 0;
 #pragma unroll
         for (int k = 0; k < 32; k += 2) {
-          const float ps0 = ex2(fmaf(x[k], cs, -ms_new));
-          const float ps1 = ex2(fmaf(x[k + 1], cs, -ms_new));
-          const float pt0 = ex2(fmaf(y[k], ct, -mt_new));
-          const float pt1 = ex2(fmaf(y[k + 1], ct, -mt_new));
-          ls0 += ps0;
-          ls1 += ps1;
-          lt0 += pt0;
-          lt1 += pt1;
-          // pt * (st - ss); masked entries have pt = 0 and a finite stand-in difference
-          const float d0 = (pt0 > 0.f) ? fmaf(y[k], p.sc_t, -x[k] * p.sc_s) : 0.f;
-          const float d1 = (pt1 > 0.f) ? fmaf(y[k + 1], p.sc_t, -x[k + 1] * p.sc_s) : 0.f;
-          a0 = fmaf(pt0, d0, a0);
-          a1 = fmaf(pt1, d1, a1);
+          const uint64_t xx = f2pack(x[k], x[k + 1]), yy = f2pack(y[k], y[k + 1]);
+          float a0, a1, b0, b1;
+          f2unpack(ffma2(xx, cs2, nms2), a0, a1);
+          f2unpack(ffma2(yy, ct2, nmt2), b0, b1);
+          float ps0, ps1, pt0, pt1;
+          if (full) {
+            ps0 = ex2_mix<kPolyEveryFwd, 4>(a0, 2 * k);
+            ps1 = ex2_mix<kPolyEveryFwd, 4>(a1, 2 * k + 2);
+            pt0 = ex2_mix<kPolyEveryFwd, 4>(b0, 2 * k + 1);
+            pt1 = ex2_mix<kPolyEveryFwd, 4>(b1, 2 * k + 3);
+          } else {
+            ps0 = ex2(a0);
+            ps1 = ex2(a1);
+            pt0 = ex2(b0);
+            pt1 = ex2(b1);
+          }
+          const uint64_t ps = f2pack(ps0, ps1), pt = f2pack(pt0, pt1);
+          ls2 = fadd2(ls2, ps);
+          lt2 = fadd2(lt2, pt);
+          ay2 = ffma2(pt, yy, ay2);
+          ax2 = ffma2(pt, xx, ax2);
         }
+        float ls0, ls1, lt0, lt1, ay0, ay1, ax0, ax1;
+        f2unpack(ls2, ls0, ls1);
+        f2unpack(lt2, lt0, lt1);
+        f2unpack(ay2, ay0, ay1);
+        f2unpack(ax2, ax0, ax1);
         l_s += ls0 + ls1;
         l_t += lt0 + lt1;
-        acc += a0 + a1;
+        ay += ay0 + ay1;
+        ax += ax0 + ax1;
         m_s = ms_new;
         m_t = mt_new;
       }
     }
+    // sum_j pt_j (st_j - ss_j) = sc_t * ay - sc_s * ax (pt not yet normalised)
+    const float acc = fmaf(p.sc_t, ay, -p.sc_s * ax);
 
-    // combine the two warpgroups' statistics of each row
-    if (wg == 1) {
-      stat[0][r] = m_s;
-      stat[1][r] = l_s;
-      stat[2][r] = m_t;
-      stat[3][r] = l_t;
-      stat[4][r] = acc;
+    // combine the four warpgroups' statistics of each row
+    if (wg > 0) {
+      float* st5 = stat + (wg - 1) * 5 * kBM;
+      st5[0 * kBM + r] = m_s;
+      st5[1 * kBM + r] = l_s;
+      st5[2 * kBM + r] = m_t;
+      st5[3 * kBM + r] = l_t;
+      st5[4 * kBM + r] = acc;
     }
-    named_bar(1, 256);
+    named_bar(1, 32 * kRowWarps);
     if (wg == 0) {
-      const float m_s2 = stat[0][r], l_s2 = stat[1][r];
-      const float m_t2 = stat[2][r], l_t2 = stat[3][r], acc2 = stat[4][r];
-      const float Ms = fmaxf(m_s, m_s2), Mt = fmaxf(m_t, m_t2);
+      float Ms = m_s, Mt = m_t;
+#pragma unroll
+      for (int g = 0; g < 3; ++g) {
+        Ms = fmaxf(Ms, stat[(g * 5 + 0) * kBM + r]);
+        Mt = fmaxf(Mt, stat[(g * 5 + 2) * kBM + r]);
+      }
       float Ls = 0.f, Lt = 0.f, A = 0.f;
-      if (Ms != -CUDART_INF_F) Ls = l_s * ex2(m_s - Ms) + l_s2 * ex2(m_s2 - Ms);
+      if (Ms != -CUDART_INF_F) {
+        Ls = l_s * ex2(m_s - Ms);
+#pragma unroll
+        for (int g = 0; g < 3; ++g)
+          Ls += stat[(g * 5 + 1) * kBM + r] * ex2(stat[(g * 5 + 0) * kBM + r] - Ms);
+      }
       if (Mt != -CUDART_INF_F) {
-        const float f1 = ex2(m_t - Mt), f2 = ex2(m_t2 - Mt);
-        Lt = l_t * f1 + l_t2 * f2;
-        A = acc * f1 + acc2 * f2;
+        const float f0 = ex2(m_t - Mt);
+        Lt = l_t * f0;
+        A = acc * f0;
+#pragma unroll
+        for (int g = 0; g < 3; ++g) {
+          const float f = ex2(stat[(g * 5 + 2) * kBM + r] - Mt);
+          Lt += stat[(g * 5 + 3) * kBM + r] * f;
+          A += stat[(g * 5 + 4) * kBM + r] * f;
+        }
       }
       const float lse_sv = (Ls > 0.f) ? (Ms + lg2(Ls)) * kLn2 : -CUDART_INF_F;
       const float lse_tv = (Lt > 0.f) ? (Mt + lg2(Lt)) * kLn2 : -CUDART_INF_F;
@@ -360,7 +444,7 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs,
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -403,9 +487,9 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, int bf16) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Per-row exponent offsets (lse_s, lse_t) * log2(e), or +inf for rows that take
-// no gradient (padding mask, non-finite LSE): e^{s - inf} = 0 removes them
-// without a branch.
+// Per-row exponent offsets -(lse_s, lse_t) * log2(e), or -inf for rows that
+// take no gradient (padding mask, non-finite LSE): e^{s - inf} = 0 removes
+// them without a branch.
 __global__ void scale_lse_kernel(const float* __restrict__ lse_s, const float* __restrict__ lse_t,
                                  const uint32_t* __restrict__ bits, int B, int Hq, int T,
                                  float2* __restrict__ out) {
@@ -417,25 +501,27 @@ __global__ void scale_lse_kernel(const float* __restrict__ lse_s, const float* _
     const int b = (int)(idx / T) / Hq;
     const float ls = lse_s[idx], lt = lse_t[idx];
     const bool ok = token_valid(bits, words, b, i) && isfinite(ls) && isfinite(lt);
-    out[idx] = ok ? make_float2(ls * kLog2e, lt * kLog2e)
-                  : make_float2(CUDART_INF_F, CUDART_INF_F);
+    out[idx] = ok ? make_float2(-ls * kLog2e, -lt * kLog2e)
+                  : make_float2(-CUDART_INF_F, -CUDART_INF_F);
   }
 }
 
-// DS/2 fp32 columns of this thread's TMEM lane, times `scale`, into
-// row_ptr[0 .. DS/2): stored, or added to what is there (read-modify-write by
+// NC fp32 columns of this thread's TMEM lane, times `scale`, into
+// row_ptr[0 .. NC): stored, or added to what is there (read-modify-write by
 // the row's only owner).
-template <int DS>
+template <int NC>
 __device__ __forceinline__ void store_rows(uint32_t taddr, float* row_ptr, float scale,
                                            bool do_store, bool accumulate) {
+  constexpr int W = NC < 32 ? NC : 32;
 #pragma unroll
-  for (int c = 0; c < DS / 2; c += 32) {
+  for (int c = 0; c < NC; c += W) {
     float v[32];
-    tmem_ld32(taddr + c, v);
+    if (W == 32) tmem_ld32(taddr + c, v);
+    else tmem_ld16(taddr + c, v);
     tmem_wait_ld();
     if (do_store) {
 #pragma unroll
-      for (int k = 0; k < 32; k += 4) {
+      for (int k = 0; k < W; k += 4) {
         float4* dst = reinterpret_cast<float4*>(row_ptr + c + k);
         float4 f = make_float4(v[k] * scale, v[k + 1] * scale, v[k + 2] * scale, v[k + 3] * scale);
         if (accumulate) {
@@ -495,7 +581,7 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
     bh0 = bh;
   }
 
-  if (warp == 0 && lane == 0) {
+  if (warp == kProducerWarp && lane == 0) {
     tma_prefetch_desc(&tm_qs);
     tma_prefetch_desc(&tm_ks);
     tma_prefetch_desc(&tm_qt);
@@ -504,7 +590,7 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
   setup_cta<L>(misc, warp, lane);
   const uint32_t tmem = misc->tmem_base;
 
-  if (warp == 0) {
+  if (warp == kProducerWarp) {
     if (lane == 0) {
       // ---------------- TMA producer
       mbar_arrive_expect_tx(&misc->q_full, L::QS + L::QT);
@@ -532,7 +618,7 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     if (lane == 0) {
       // ---------------- MMA issuer: scores of step j+1 ahead of the gradient GEMM of j
       const uint32_t id_s = idesc_f16(kBM, kBN, p.dtype_s, p.dtype_s, 0, 0);
@@ -579,10 +665,10 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
         umma_commit(&misc->k_empty[s]);
       }
     }
-  } else if (warp >= 4) {
-    // ---------------- row warps: lane r of the stationary tile, 64 streamed
+  } else if (warp < kRowWarps) {
+    // ---------------- row warps: lane r of the stationary tile, 32 streamed
     // columns (of each 128) per warpgroup
-    const int wg = (warp - 4) >> 2, q = warp & 3;
+    const int wg = warp >> 2, q = warp & 3;
     const int r = q * 32 + lane;
     const int words = (p.T + 31) >> 5;
     const int own = st_tile * kBM + r;  // query row (dq) or key row (dk) of this lane
@@ -590,56 +676,63 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
     const float cs = p.sc_s * kLog2e, ct = p.sc_t * kLog2e;
     const float gscale = p.sc_s * (dloss ? *dloss : 1.f);
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
-    uint8_t* del_row = smem + L::OFF_DEL + wg * kChunk + r * 128;
+    // this warpgroup's 32 columns = half of a 128-byte swizzle row of chunk wg/2
+    uint8_t* del_row = smem + L::OFF_DEL + (wg >> 1) * kChunk + r * 128;
     // dq: this row's exponent offsets; dk: whether this key takes part at all
-    float2 Lrow = make_float2(CUDART_INF_F, CUDART_INF_F);
+    float2 Lrow = make_float2(-CUDART_INF_F, -CUDART_INF_F);
     bool key_ok = true;
     if (!DK) {
       if (own_in) Lrow = lsc[(size_t)bh0 * p.T + own];
     } else {
       key_ok = own_in && token_valid(bits, words, b, own);
     }
-    const bool row_live = DK ? key_ok : (Lrow.x != CUDART_INF_F);
+    const bool row_live = DK ? key_ok : (Lrow.x != -CUDART_INF_F);
+    const uint64_t cs2 = f2pack(cs, cs), ct2 = f2pack(ct, ct);
+    const uint64_t nls2 = f2pack(Lrow.x, Lrow.x), nlt2 = f2pack(Lrow.y, Lrow.y);
 
     for (int j = 0; j < n_steps; ++j) {
       const int tile = first_tile + j % n_per_head;
       // dk: lane k fetches the exponent offsets of columns k and 32 + k of this
       // warpgroup's 64 query rows before the scores arrive; they are handed to
       // the other lanes with shuffles
-      float2 lA = make_float2(0.f, 0.f), lB = make_float2(0.f, 0.f);
+      float2 lA = make_float2(0.f, 0.f);
       if (DK) {
         const float2* lcol = lsc + (size_t)(bh0 + j / n_per_head) * p.T;
-        const int cb = tile * kBN + wg * 64 + lane;
-        lA = lcol[min(cb, p.T - 1)];
-        lB = lcol[min(cb + 32, p.T - 1)];
+        lA = lcol[min(tile * kBN + wg * 32 + lane, p.T - 1)];
       }
       if (!mbar_wait(&misc->s_full[0], j & 1, abort, err)) break;
       tc_fence_after();
-      uint32_t packed[32];
-      // load all 64 ss and 64 st values of this thread first and release the
-      // (single) score buffer at once, so the next tile's score GEMMs run
-      // under this tile's exponentials
-      float xa[2][32], ya[2][32];
-      tmem_ld32(lane_addr + wg * 64, xa[0]);
-      tmem_ld32(lane_addr + 128 + wg * 64, ya[0]);
-      tmem_ld32(lane_addr + wg * 64 + 32, xa[1]);
-      tmem_ld32(lane_addr + 128 + wg * 64 + 32, ya[1]);
+      uint32_t packed[16];
+      // load this thread's 32 ss and 32 st values and release the (single)
+      // score buffer at once, so the next tile's score GEMMs run under this
+      // tile's exponentials
+      float xa[1][32], ya[1][32];
+      tmem_ld32(lane_addr + wg * 32, xa[0]);
+      tmem_ld32(lane_addr + 128 + wg * 32, ya[0]);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&misc->s_empty[0]);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
+      for (int half = 0; half < 1; ++half) {
         float(&x)[32] = xa[half];
         float(&y)[32] = ya[half];
-        const int c0 = tile * kBN + wg * 64 + half * 32;  // first streamed row of these columns
+        const int c0 = tile * kBN + wg * 32;  // first streamed row of these columns
         // (no early exit for dead rows: the dk branch shuffles across the warp)
         float d[32];
         bool full;
         if (!DK) {
 #pragma unroll
-          for (int k = 0; k < 32; ++k)
-            d[k] = ex2(fmaf(x[k], cs, -Lrow.x)) - ex2(fmaf(y[k], ct, -Lrow.y));
+          for (int k = 0; k < 32; k += 2) {
+            float a0, a1, b0, b1;
+            f2unpack(ffma2(f2pack(x[k], x[k + 1]), cs2, nls2), a0, a1);
+            f2unpack(ffma2(f2pack(y[k], y[k + 1]), ct2, nlt2), b0, b1);
+            const uint64_t e = fsub2(f2pack(ex2_mix<kPolyEveryBwd, 3>(a0, 2 * k),
+                                            ex2_mix<kPolyEveryBwd, 3>(a1, 2 * k + 2)),
+                                     f2pack(ex2_mix<kPolyEveryBwd, 3>(b0, 2 * k + 1),
+                                            ex2_mix<kPolyEveryBwd, 3>(b1, 2 * k + 3)));
+            f2unpack(e, d[k], d[k + 1]);
+          }
           // columns are keys c: valid iff c <= i (causal), c < T, key not padded
           const int lim = p.causal ? min(own, p.T - 1) : p.T - 1;
           full = (c0 + 31 <= lim) && (bits == nullptr);
@@ -649,15 +742,24 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
               if (!((c0 + k <= lim) && token_valid(bits, words, b, c0 + k))) d[k] = 0.f;
           }
         } else {
-          const float2 lh = half ? lB : lA;
+          const float2 lh = lA;
 #pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const float lx = __shfl_sync(0xffffffffu, lh.x, k);
-            const float ly = __shfl_sync(0xffffffffu, lh.y, k);
-            d[k] = ex2(fmaf(x[k], cs, -lx)) - ex2(fmaf(y[k], ct, -ly));
+          for (int k = 0; k < 32; k += 2) {
+            const uint64_t nl_s = f2pack(__shfl_sync(0xffffffffu, lh.x, k),
+                                         __shfl_sync(0xffffffffu, lh.x, k + 1));
+            const uint64_t nl_t = f2pack(__shfl_sync(0xffffffffu, lh.y, k),
+                                         __shfl_sync(0xffffffffu, lh.y, k + 1));
+            float a0, a1, b0, b1;
+            f2unpack(ffma2(f2pack(x[k], x[k + 1]), cs2, nl_s), a0, a1);
+            f2unpack(ffma2(f2pack(y[k], y[k + 1]), ct2, nl_t), b0, b1);
+            const uint64_t e = fsub2(f2pack(ex2_mix<kPolyEveryBwd, 3>(a0, 2 * k),
+                                            ex2_mix<kPolyEveryBwd, 3>(a1, 2 * k + 2)),
+                                     f2pack(ex2_mix<kPolyEveryBwd, 3>(b0, 2 * k + 1),
+                                            ex2_mix<kPolyEveryBwd, 3>(b1, 2 * k + 3)));
+            f2unpack(e, d[k], d[k + 1]);
           }
           // columns are query rows c: valid iff c >= j (causal) and c < T; padded
-          // or LSE-less rows carry +inf offsets and give 0 by themselves
+          // or LSE-less rows carry -inf offsets and give 0 by themselves
           full = (!p.causal || c0 >= own) && (c0 + 31 < p.T);
           if (!full) {
 #pragma unroll
@@ -675,12 +777,13 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
       if (j > 0) {
         if (!mbar_wait(&misc->d_empty, (j - 1) & 1, abort, err)) break;
       }
-      // D row r (64 columns of chunk wg): 8 x 16 B pieces, 128B-swizzled
+      // D row r, this warpgroup's 32 columns: 4 x 16 B pieces of the 128B-swizzled row
 #pragma unroll
-      for (int pc = 0; pc < 8; ++pc) {
+      for (int pc = 0; pc < 4; ++pc) {
         uint4 v = make_uint4(packed[pc * 4], packed[pc * 4 + 1], packed[pc * 4 + 2],
                              packed[pc * 4 + 3]);
-        *reinterpret_cast<uint4*>(del_row + ((pc ^ (r & 7)) << 4)) = v;
+        const int piece = (wg & 1) * 4 + pc;
+        *reinterpret_cast<uint4*>(del_row + ((piece ^ (r & 7)) << 4)) = v;
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -690,14 +793,14 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
       tc_fence_after();
       float* row = DK ? out + (((size_t)b * p.Hkv_s + hs) * p.T + own) * DS
                       : out + ((size_t)bh0 * p.T + own) * DS;
-      store_rows<DS>(lane_addr + kColAcc + wg * (DS / 2), row + wg * (DS / 2), gscale, own_in,
+      store_rows<DS / 4>(lane_addr + kColAcc + wg * (DS / 4), row + wg * (DS / 4), gscale, own_in,
                      DK && accumulate != 0);
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
