@@ -55,47 +55,6 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// 2^x on the FMA pipe, for part of the exponentials (the MUFU unit that
-// serves ex2.approx delivers 16 results per clock per SM and is the shared
-// bound of every kernel here).  Cody-Waite style reduction: x = j + f with j
-// the nearest integer (added into the exponent bits) and f in [-1/2, 1/2],
-// then 2^f by a polynomial fitted here for minimum relative error on that
-// interval (Remez exchange in double precision):
-//   degree 3: max relative error 7.5e-5 (fp32 Horner); degree 4: 2.7e-6.
-// Inputs below -125 are clamped (result ~2e-38 instead of 0); callers use it
-// only where the argument is <= 0 and finite, or where tiny results are
-// harmless.
-template <int DEG>
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -125.0f);
-  const float t = __fadd_rn(x, 12582912.0f);  // 1.5 * 2^23: round to nearest integer
-  const float j = __fadd_rn(t, -12582912.0f);
-  const float f = __fadd_rn(x, -j);
-  float p;
-  if (DEG == 3) {
-    p = fmaf(5.517166907e-02f, f, 2.426111222e-01f);
-    p = fmaf(p, f, 6.932609855e-01f);
-    p = fmaf(p, f, 9.999280735e-01f);
-  } else {
-    p = fmaf(9.570101908e-03f, f, 5.591786032e-02f);
-    p = fmaf(p, f, 2.402474483e-01f);
-    p = fmaf(p, f, 6.931218147e-01f);
-    p = fmaf(p, f, 9.999992614e-01f);
-  }
-  const int ji = __float_as_int(t) - 0x4B400000;
-  return __int_as_float(__float_as_int(p) + (ji << 23));
-}
-
-// Exponentials of element k of a 32-element chunk: every kPolyEvery-th one on
-// the FMA pipe (0 = none).
-template <int EVERY, int DEG>
-__device__ __forceinline__ float ex2_mix(float x, int k) {
-  if (EVERY > 0 && (k % EVERY) == EVERY - 1) return ex2_poly<DEG>(x);
-  return ex2(x);
-}
-constexpr int kPolyEveryFwd = 0;
-constexpr int kPolyEveryBwd = 0;
-
 __device__ __forceinline__ float lg2(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -355,18 +314,7 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs,
           float a0, a1, b0, b1;
           f2unpack(ffma2(xx, cs2, nms2), a0, a1);
           f2unpack(ffma2(yy, ct2, nmt2), b0, b1);
-          float ps0, ps1, pt0, pt1;
-          if (full) {
-            ps0 = ex2_mix<kPolyEveryFwd, 4>(a0, 2 * k);
-            ps1 = ex2_mix<kPolyEveryFwd, 4>(a1, 2 * k + 2);
-            pt0 = ex2_mix<kPolyEveryFwd, 4>(b0, 2 * k + 1);
-            pt1 = ex2_mix<kPolyEveryFwd, 4>(b1, 2 * k + 3);
-          } else {
-            ps0 = ex2(a0);
-            ps1 = ex2(a1);
-            pt0 = ex2(b0);
-            pt1 = ex2(b1);
-          }
+          const float ps0 = ex2(a0), ps1 = ex2(a1), pt0 = ex2(b0), pt1 = ex2(b1);
           const uint64_t ps = f2pack(ps0, ps1), pt = f2pack(pt0, pt1);
           ls2 = fadd2(ls2, ps);
           lt2 = fadd2(lt2, pt);
@@ -727,10 +675,7 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
             float a0, a1, b0, b1;
             f2unpack(ffma2(f2pack(x[k], x[k + 1]), cs2, nls2), a0, a1);
             f2unpack(ffma2(f2pack(y[k], y[k + 1]), ct2, nlt2), b0, b1);
-            const uint64_t e = fsub2(f2pack(ex2_mix<kPolyEveryBwd, 3>(a0, 2 * k),
-                                            ex2_mix<kPolyEveryBwd, 3>(a1, 2 * k + 2)),
-                                     f2pack(ex2_mix<kPolyEveryBwd, 3>(b0, 2 * k + 1),
-                                            ex2_mix<kPolyEveryBwd, 3>(b1, 2 * k + 3)));
+            const uint64_t e = fsub2(f2pack(ex2(a0), ex2(a1)), f2pack(ex2(b0), ex2(b1)));
             f2unpack(e, d[k], d[k + 1]);
           }
           // columns are keys c: valid iff c <= i (causal), c < T, key not padded
@@ -752,10 +697,7 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
             float a0, a1, b0, b1;
             f2unpack(ffma2(f2pack(x[k], x[k + 1]), cs2, nl_s), a0, a1);
             f2unpack(ffma2(f2pack(y[k], y[k + 1]), ct2, nl_t), b0, b1);
-            const uint64_t e = fsub2(f2pack(ex2_mix<kPolyEveryBwd, 3>(a0, 2 * k),
-                                            ex2_mix<kPolyEveryBwd, 3>(a1, 2 * k + 2)),
-                                     f2pack(ex2_mix<kPolyEveryBwd, 3>(b0, 2 * k + 1),
-                                            ex2_mix<kPolyEveryBwd, 3>(b1, 2 * k + 3)));
+            const uint64_t e = fsub2(f2pack(ex2(a0), ex2(a1)), f2pack(ex2(b0), ex2(b1)));
             f2unpack(e, d[k], d[k + 1]);
           }
           // columns are query rows c: valid iff c >= j (causal) and c < T; padded
