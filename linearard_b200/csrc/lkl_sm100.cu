@@ -83,16 +83,22 @@ struct FwdLayout {
   static_assert(NS >= 2, "forward needs two K stages");
 };
 
+
+// Gradient kernels: the stationary tiles pass through shared memory only
+// once (they are copied into TMEM), so they borrow the last K stage slot and
+// the streamed tiles get NS stages.
 template <int DS, int DT>
-struct BwdLayout {
+struct GradLayout {
   static constexpr int QS = kBM * DS * 2, QT = kBM * DT * 2, DEL = kBM * kBN * 2;
   static constexpr int STAGE = kBN * (DS + DT) * 2;
-  static constexpr int AVAIL = kMaxDynSmem - 1024 - kMisc - QS - QT - DEL;
-  static constexpr int NS = (AVAIL / STAGE) >= 3 ? 3 : (AVAIL / STAGE);
-  static constexpr int OFF_QS = 0, OFF_QT = QS, OFF_DEL = QS + QT, OFF_K = QS + QT + DEL;
+  static constexpr int AVAIL = kMaxDynSmem - 1024 - kMisc - DEL;
+  static constexpr int NS = (AVAIL / STAGE) >= 4 ? 4 : (AVAIL / STAGE);
+  static constexpr int OFF_DEL = 0, OFF_K = DEL;
+  static constexpr int OFF_QS = OFF_K + (NS - 1) * STAGE, OFF_QT = OFF_QS + QS;
   static constexpr int OFF_MISC = OFF_K + NS * STAGE;
   static constexpr int BYTES = 1024 + OFF_MISC + kMisc;
-  static_assert(NS >= 2, "backward needs two K stages");
+  static_assert(NS >= 3, "gradient kernels need three K stages");
+  static_assert(QS + QT <= STAGE, "stationary tiles must fit one stage");
 };
 
 struct Misc {
@@ -103,6 +109,7 @@ struct Misc {
   uint64_t s_empty[2];
   uint64_t d_full;
   uint64_t d_empty;
+  uint64_t a_ready;  // gradient kernels: stationary tile copied into TMEM
   uint32_t tmem_base;
   int abort;
   float red[8];
@@ -162,6 +169,7 @@ __device__ __forceinline__ void setup_cta(Misc* misc, int warp, int lane) {
     }
     mbar_init(&misc->d_full, kRowWarps);
     mbar_init(&misc->d_empty, 1);
+    mbar_init(&misc->a_ready, 4);
     misc->abort = 0;
     fence_barrier_init();
   }
@@ -267,7 +275,8 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs,
         const uint32_t col = bf * 256 + wg * 32;
         tmem_ld32(lane_addr + col, x);
         tmem_ld32(lane_addr + col + 128, y);
-        tmem_wait_ld();
+        tmem_wait_ld_dep(x);
+        tmem_wait_ld_dep(y);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&misc->s_empty[bf]);
@@ -466,7 +475,7 @@ __device__ __forceinline__ void store_rows(uint32_t taddr, float* row_ptr, float
     float v[32];
     if (W == 32) tmem_ld32(taddr + c, v);
     else tmem_ld16(taddr + c, v);
-    tmem_wait_ld();
+    tmem_wait_ld_dep(v);
     if (do_store) {
 #pragma unroll
       for (int k = 0; k < W; k += 4) {
@@ -485,6 +494,27 @@ __device__ __forceinline__ void store_rows(uint32_t taddr, float* row_ptr, float
   }
 }
 
+// Row r of a [128][D] 16-bit tile stored as 128B-swizzled [128][64] chunks
+// -> TMEM lane r, D/2 columns, two elements per column in K order: the
+// layout tcgen05.mma reads an A operand from.
+template <int D>
+__device__ __forceinline__ void tile_row_to_tmem(const uint8_t* tile, int r, uint32_t taddr) {
+#pragma unroll
+  for (int c = 0; c < D / 64; ++c) {
+    uint32_t v[32];
+    const uint8_t* row = tile + c * kChunk + r * 128;
+#pragma unroll
+    for (int pc = 0; pc < 8; ++pc) {
+      const uint4 q = *reinterpret_cast<const uint4*>(row + ((pc ^ (r & 7)) << 4));
+      v[pc * 4 + 0] = q.x;
+      v[pc * 4 + 1] = q.y;
+      v[pc * 4 + 2] = q.z;
+      v[pc * 4 + 3] = q.w;
+    }
+    tmem_st32(taddr + c * 32, v);
+  }
+}
+
 template <int DS, int DT, bool DK, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
 sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
@@ -493,7 +523,7 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
                   const __grid_constant__ CUtensorMap tm_kt, const Problem p,
                   const float2* __restrict__ lsc, const uint32_t* __restrict__ bits,
                   const float* __restrict__ dloss, float* out, int accumulate) {
-  using L = BwdLayout<DS, DT>;  // stationary tiles at OFF_QS / OFF_QT, streamed in stages
+  using L = GradLayout<DS, DT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   Misc* misc = reinterpret_cast<Misc*>(smem + L::OFF_MISC);
@@ -501,6 +531,10 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
   int* err = &g_device_error;
   volatile int* abort = &misc->abort;
   constexpr uint32_t kColAcc = 256;
+  // the stationary student / teacher tiles live in TMEM as A operands of the
+  // score GEMMs, so those GEMMs read only their B operand from shared memory
+  constexpr uint32_t kColAs = kColAcc + DS, kColAt = kColAs + DS / 2;
+  static_assert(kColAt + DT / 2 <= kTmemCols, "TMEM budget");
 
   // ---- work of this CTA (head-major, longest first)
   const int n_t = (p.T + kBM - 1) / kBM;
@@ -552,6 +586,8 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
       for (int j = 0; j < n_steps; ++j) {
         const int s = j % L::NS;
         if (j >= L::NS && !mbar_wait(&misc->k_empty[s], ((j / L::NS) - 1) & 1, abort, err)) break;
+        // the last slot first holds the stationary tiles until they are in TMEM
+        if (j == L::NS - 1 && !mbar_wait(&misc->a_ready, 0, abort, err)) break;
         uint8_t* stg = smem + L::OFF_K + s * L::STAGE;
         mbar_arrive_expect_tx(&misc->k_full[s], L::STAGE);
         const int tile = first_tile + j % n_per_head;
@@ -572,7 +608,6 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
       const uint32_t id_s = idesc_f16(kBM, kBN, p.dtype_s, p.dtype_s, 0, 0);
       const uint32_t id_t = idesc_f16(kBM, kBN, p.dtype_t, p.dtype_t, 0, 0);
       const uint32_t id_g = idesc_f16(kBM, DS, p.dtype_s, p.dtype_s, 0, 1);
-      const uint32_t a_s = smem_u32(smem + L::OFF_QS), a_t = smem_u32(smem + L::OFF_QT);
       const uint32_t a_d = smem_u32(smem + L::OFF_DEL);
       auto issue_scores = [&](int j) {
         const int s = j % L::NS;
@@ -580,13 +615,13 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
         const uint32_t b_t = b_s + kBN * DS * 2;
 #pragma unroll
         for (int kk = 0; kk < DS / 16; ++kk)
-          umma_f16_ss(tmem, kmajor_desc(a_s, kk), kmajor_desc(b_s, kk), id_s, kk > 0);
+          umma_f16_ts(tmem, tmem + kColAs + kk * 8, kmajor_desc(b_s, kk), id_s, kk > 0);
 #pragma unroll
         for (int kk = 0; kk < DT / 16; ++kk)
-          umma_f16_ss(tmem + 128, kmajor_desc(a_t, kk), kmajor_desc(b_t, kk), id_t, kk > 0);
+          umma_f16_ts(tmem + 128, tmem + kColAt + kk * 8, kmajor_desc(b_t, kk), id_t, kk > 0);
         umma_commit(&misc->s_full[0]);
       };
-      bool ok = mbar_wait(&misc->q_full, 0, abort, err) &&
+      bool ok = mbar_wait(&misc->a_ready, 0, abort, err) &&
                 mbar_wait(&misc->k_full[0], 0, abort, err);
       if (ok) {
         tc_fence_after();
@@ -635,6 +670,17 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
       key_ok = own_in && token_valid(bits, words, b, own);
     }
     const bool row_live = DK ? key_ok : (Lrow.x != -CUDART_INF_F);
+    if (wg == 0) {
+      // warpgroup 0 moves the stationary tiles (all 128 rows) into TMEM
+      if (mbar_wait(&misc->q_full, 0, abort, err)) {
+        tile_row_to_tmem<DS>(smem + L::OFF_QS, r, lane_addr + kColAs);
+        tile_row_to_tmem<DT>(smem + L::OFF_QT, r, lane_addr + kColAt);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&misc->a_ready);
+    }
     const uint64_t cs2 = f2pack(cs, cs), ct2 = f2pack(ct, ct);
     const uint64_t nls2 = f2pack(Lrow.x, Lrow.x), nlt2 = f2pack(Lrow.y, Lrow.y);
 
@@ -654,30 +700,32 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
       // load this thread's 32 ss and 32 st values and release the (single)
       // score buffer at once, so the next tile's score GEMMs run under this
       // tile's exponentials
-      float xa[1][32], ya[1][32];
-      tmem_ld32(lane_addr + wg * 32, xa[0]);
-      tmem_ld32(lane_addr + 128 + wg * 32, ya[0]);
-      tmem_wait_ld();
+      float x[32], y[32];
+      tmem_ld32(lane_addr + wg * 32, x);
+      tmem_ld32(lane_addr + 128 + wg * 32, y);
+      tmem_wait_ld_dep(x);
+      tmem_wait_ld_dep(y);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&misc->s_empty[0]);
-#pragma unroll
-      for (int half = 0; half < 1; ++half) {
-        float(&x)[32] = xa[half];
-        float(&y)[32] = ya[half];
+      {
         const int c0 = tile * kBN + wg * 32;  // first streamed row of these columns
         // (no early exit for dead rows: the dk branch shuffles across the warp)
         float d[32];
+#pragma unroll
+        for (int k = 0; k < 32; k += 2) {
+          uint64_t nl_s = nls2, nl_t = nlt2;
+          if (DK) {
+            nl_s = f2pack(__shfl_sync(0xffffffffu, lA.x, k), __shfl_sync(0xffffffffu, lA.x, k + 1));
+            nl_t = f2pack(__shfl_sync(0xffffffffu, lA.y, k), __shfl_sync(0xffffffffu, lA.y, k + 1));
+          }
+          float a0, a1, b0, b1;
+          f2unpack(ffma2(f2pack(x[k], x[k + 1]), cs2, nl_s), a0, a1);
+          f2unpack(ffma2(f2pack(y[k], y[k + 1]), ct2, nl_t), b0, b1);
+          f2unpack(fsub2(f2pack(ex2(a0), ex2(a1)), f2pack(ex2(b0), ex2(b1))), d[k], d[k + 1]);
+        }
         bool full;
         if (!DK) {
-#pragma unroll
-          for (int k = 0; k < 32; k += 2) {
-            float a0, a1, b0, b1;
-            f2unpack(ffma2(f2pack(x[k], x[k + 1]), cs2, nls2), a0, a1);
-            f2unpack(ffma2(f2pack(y[k], y[k + 1]), ct2, nlt2), b0, b1);
-            const uint64_t e = fsub2(f2pack(ex2(a0), ex2(a1)), f2pack(ex2(b0), ex2(b1)));
-            f2unpack(e, d[k], d[k + 1]);
-          }
           // columns are keys c: valid iff c <= i (causal), c < T, key not padded
           const int lim = p.causal ? min(own, p.T - 1) : p.T - 1;
           full = (c0 + 31 <= lim) && (bits == nullptr);
@@ -687,19 +735,6 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
               if (!((c0 + k <= lim) && token_valid(bits, words, b, c0 + k))) d[k] = 0.f;
           }
         } else {
-          const float2 lh = lA;
-#pragma unroll
-          for (int k = 0; k < 32; k += 2) {
-            const uint64_t nl_s = f2pack(__shfl_sync(0xffffffffu, lh.x, k),
-                                         __shfl_sync(0xffffffffu, lh.x, k + 1));
-            const uint64_t nl_t = f2pack(__shfl_sync(0xffffffffu, lh.y, k),
-                                         __shfl_sync(0xffffffffu, lh.y, k + 1));
-            float a0, a1, b0, b1;
-            f2unpack(ffma2(f2pack(x[k], x[k + 1]), cs2, nl_s), a0, a1);
-            f2unpack(ffma2(f2pack(y[k], y[k + 1]), ct2, nl_t), b0, b1);
-            const uint64_t e = fsub2(f2pack(ex2(a0), ex2(a1)), f2pack(ex2(b0), ex2(b1)));
-            f2unpack(e, d[k], d[k + 1]);
-          }
           // columns are query rows c: valid iff c >= j (causal) and c < T; padded
           // or LSE-less rows carry -inf offsets and give 0 by themselves
           full = (!p.causal || c0 >= own) && (c0 + 31 < p.T);
@@ -714,7 +749,7 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
           for (int k = 0; k < 32; ++k) d[k] = 0.f;
         }
 #pragma unroll
-        for (int k = 0; k < 32; k += 2) packed[half * 16 + (k >> 1)] = pack2t<BF16>(d[k], d[k + 1]);
+        for (int k = 0; k < 32; k += 2) packed[k >> 1] = pack2t<BF16>(d[k], d[k + 1]);
       }
       if (j > 0) {
         if (!mbar_wait(&misc->d_empty, (j - 1) & 1, abort, err)) break;
@@ -816,7 +851,7 @@ cudaError_t run_forward(const Problem& p, const Maps& m, const uint32_t* bits, f
 template <int DS, int DT>
 cudaError_t run_grad(const Problem& p, const Maps& m, const float2* lsc, const uint32_t* bits,
                      const float* dloss, float* dq, float* dk, bool alias, cudaStream_t st) {
-  using L = BwdLayout<DS, DT>;
+  using L = GradLayout<DS, DT>;
   const bool bf = p.dtype_s == LKL_BF16;
   auto kq = bf ? sm100_grad_kernel<DS, DT, false, true> : sm100_grad_kernel<DS, DT, false, false>;
   auto kk = bf ? sm100_grad_kernel<DS, DT, true, true> : sm100_grad_kernel<DS, DT, true, false>;
