@@ -84,21 +84,21 @@ struct FwdLayout {
 };
 
 
-// Gradient kernels: the stationary tiles pass through shared memory only
-// once (they are copied into TMEM), so they borrow the last K stage slot and
-// the streamed tiles get NS stages.
+// Gradient kernels: the stationary student tile passes through shared memory
+// only once (it is copied into TMEM), so it borrows the last stage slot; the
+// stationary teacher tile stays in shared memory; D lives in TMEM.
 template <int DS, int DT>
 struct GradLayout {
-  static constexpr int QS = kBM * DS * 2, QT = kBM * DT * 2, DEL = kBM * kBN * 2;
+  static constexpr int QS = kBM * DS * 2, QT = kBM * DT * 2;
   static constexpr int STAGE = kBN * (DS + DT) * 2;
-  static constexpr int AVAIL = kMaxDynSmem - 1024 - kMisc - DEL;
+  static constexpr int AVAIL = kMaxDynSmem - 1024 - kMisc - QT;
   static constexpr int NS = (AVAIL / STAGE) >= 4 ? 4 : (AVAIL / STAGE);
-  static constexpr int OFF_DEL = 0, OFF_K = DEL;
-  static constexpr int OFF_QS = OFF_K + (NS - 1) * STAGE, OFF_QT = OFF_QS + QS;
+  static constexpr int OFF_QT = 0, OFF_K = QT;
+  static constexpr int OFF_QS = OFF_K + (NS - 1) * STAGE;
   static constexpr int OFF_MISC = OFF_K + NS * STAGE;
   static constexpr int BYTES = 1024 + OFF_MISC + kMisc;
   static_assert(NS >= 3, "gradient kernels need three K stages");
-  static_assert(QS + QT <= STAGE, "stationary tiles must fit one stage");
+  static_assert(QS <= STAGE, "stationary student tile must fit one stage");
 };
 
 struct Misc {
@@ -531,10 +531,10 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
   int* err = &g_device_error;
   volatile int* abort = &misc->abort;
   constexpr uint32_t kColAcc = 256;
-  // the stationary student / teacher tiles live in TMEM as A operands of the
-  // score GEMMs, so those GEMMs read only their B operand from shared memory
-  constexpr uint32_t kColAs = kColAcc + DS, kColAt = kColAs + DS / 2;
-  static_assert(kColAt + DT / 2 <= kTmemCols, "TMEM budget");
+  // TMEM: scores [0, 256), accumulator, the stationary student tile (A of the
+  // student score GEMM) and D (A of the gradient GEMM, written by the row warps)
+  constexpr uint32_t kColAs = kColAcc + DS, kColD = kColAs + DS / 2;
+  static_assert(kColD + kBN / 2 <= kTmemCols, "TMEM budget");
 
   // ---- work of this CTA (head-major, longest first)
   const int n_t = (p.T + kBM - 1) / kBM;
@@ -608,7 +608,7 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
       const uint32_t id_s = idesc_f16(kBM, kBN, p.dtype_s, p.dtype_s, 0, 0);
       const uint32_t id_t = idesc_f16(kBM, kBN, p.dtype_t, p.dtype_t, 0, 0);
       const uint32_t id_g = idesc_f16(kBM, DS, p.dtype_s, p.dtype_s, 0, 1);
-      const uint32_t a_d = smem_u32(smem + L::OFF_DEL);
+      const uint32_t a_t = smem_u32(smem + L::OFF_QT);
       auto issue_scores = [&](int j) {
         const int s = j % L::NS;
         const uint32_t b_s = smem_u32(smem + L::OFF_K + s * L::STAGE);
@@ -618,7 +618,7 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
           umma_f16_ts(tmem, tmem + kColAs + kk * 8, kmajor_desc(b_s, kk), id_s, kk > 0);
 #pragma unroll
         for (int kk = 0; kk < DT / 16; ++kk)
-          umma_f16_ts(tmem + 128, tmem + kColAt + kk * 8, kmajor_desc(b_t, kk), id_t, kk > 0);
+          umma_f16_ss(tmem + 128, kmajor_desc(a_t, kk), kmajor_desc(b_t, kk), id_t, kk > 0);
         umma_commit(&misc->s_full[0]);
       };
       bool ok = mbar_wait(&misc->a_ready, 0, abort, err) &&
@@ -639,10 +639,10 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
         tc_fence_after();
         const int s = j % L::NS;
         const uint32_t b_s = smem_u32(smem + L::OFF_K + s * L::STAGE);
-        // acc += D . X  with D K-major and X = the streamed student tile, MN-major
+        // acc += D . X  with D from TMEM and X = the streamed student tile, MN-major
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk)
-          umma_f16_ss(tmem + kColAcc, kmajor_desc(a_d, kk), mnmajor_desc(b_s, kk), id_g,
+          umma_f16_ts(tmem + kColAcc, tmem + kColD + kk * 8, mnmajor_desc(b_s, kk), id_g,
                       (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&misc->d_empty);
         umma_commit(&misc->k_empty[s]);
@@ -659,8 +659,6 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
     const float cs = p.sc_s * kLog2e, ct = p.sc_t * kLog2e;
     const float gscale = p.sc_s * (dloss ? *dloss : 1.f);
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
-    // this warpgroup's 32 columns = half of a 128-byte swizzle row of chunk wg/2
-    uint8_t* del_row = smem + L::OFF_DEL + (wg >> 1) * kChunk + r * 128;
     // dq: this row's exponent offsets; dk: whether this key takes part at all
     float2 Lrow = make_float2(-CUDART_INF_F, -CUDART_INF_F);
     bool key_ok = true;
@@ -674,7 +672,6 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
       // warpgroup 0 moves the stationary tiles (all 128 rows) into TMEM
       if (mbar_wait(&misc->q_full, 0, abort, err)) {
         tile_row_to_tmem<DS>(smem + L::OFF_QS, r, lane_addr + kColAs);
-        tile_row_to_tmem<DT>(smem + L::OFF_QT, r, lane_addr + kColAt);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -753,16 +750,12 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
       }
       if (j > 0) {
         if (!mbar_wait(&misc->d_empty, (j - 1) & 1, abort, err)) break;
+        tc_fence_after();
       }
-      // D row r, this warpgroup's 32 columns: 4 x 16 B pieces of the 128B-swizzled row
-#pragma unroll
-      for (int pc = 0; pc < 4; ++pc) {
-        uint4 v = make_uint4(packed[pc * 4], packed[pc * 4 + 1], packed[pc * 4 + 2],
-                             packed[pc * 4 + 3]);
-        const int piece = (wg & 1) * 4 + pc;
-        *reinterpret_cast<uint4*>(del_row + ((piece ^ (r & 7)) << 4)) = v;
-      }
-      fence_proxy_async_smem();
+      // D row r, this warpgroup's 32 columns -> TMEM columns [16 wg, 16 wg + 16) of D
+      tmem_st16(lane_addr + kColD + wg * 16, packed);
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&misc->d_full);
     }
