@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define LKL_ABI_VERSION 1
+#define LKL_ABI_VERSION 2
 
 /* element types of q/k tensors */
 enum lkl_dtype { LKL_F16 = 0, LKL_BF16 = 1 };
@@ -59,7 +59,7 @@ enum lkl_status {
   LKL_ERR_BAD_HEAD_DIM = 3,     /* D not in {8,16,32,64,128,256}                     */
   LKL_ERR_BAD_DTYPE = 4,        /* unknown lkl_dtype / lkl_mask_dtype                */
   LKL_ERR_MISALIGNED = 5,       /* pointer not aligned to its element size           */
-  LKL_ERR_WORKSPACE = 6,        /* workspace NULL or smaller than lkl_workspace_size */
+  LKL_ERR_WORKSPACE = 6,        /* workspace NULL or smaller than *_workspace_size  */
   LKL_ERR_LAUNCH = 7,           /* a kernel launch or driver call failed             */
   LKL_ERR_NO_DEVICE = 8,        /* current device is not sm_100 / no CUDA device     */
   LKL_ERR_DEVICE_TIMEOUT = 9,   /* a device-side bounded wait expired (see below)    */
@@ -92,6 +92,14 @@ const char* lkl_status_string(int32_t status);
  * padding mask will be passed).  Always a multiple of 256. */
 size_t lkl_workspace_size(const lkl_problem* p, int32_t has_mask);
 
+/* Bytes of scratch lkl_backward needs: lkl_workspace_size plus, for the
+ * tensor-core path (Ds, Dt in {64, 128}, Hkv_s == Hkv_t), a buffer for the
+ * 16-bit D tiles (p_s - p_t) that the dq pass hands to the dk pass: all of
+ * them up to 8 GiB, beyond that the backward runs in chunks of kv heads or of
+ * query-tile ranges (so the buffer stays bounded for any T).  A multiple of
+ * 256.  Added in ABI version 2. */
+size_t lkl_backward_workspace_size(const lkl_problem* p, int32_t has_mask);
+
 /* Row log-sum-exp of one (q, k) pair -> lse [B, Hq, T] fp32.
  * Uses (Hkv_s, Ds, dtype_s, sm_scale_s) of `p`; rows removed by the mask get 0,
  * rows with no valid column get -inf (kernel_A.py:146-158).
@@ -121,7 +129,9 @@ int32_t lkl_forward(const void* qs, const void* ks, const void* qt, const void* 
  * attn_kl_align(qs, qs, qt, qt) made by train.py:380-402), the buffer receives
  * dq + dk, the gradient of the shared tensor.
  * Replaces kl_backward_triton (kernels/attention_KL/kernel_C.py:293-449) and
- * the chain rule in AttnKLAlignFn.backward (integration.py:48-67). */
+ * the chain rule in AttnKLAlignFn.backward (integration.py:48-67).
+ * The workspace must hold lkl_backward_workspace_size(p, mask != NULL) bytes
+ * (LKL_ERR_WORKSPACE otherwise). */
 int32_t lkl_backward(const void* qs, const void* ks, const float* lse_s,
                      const void* qt, const void* kt, const float* lse_t,
                      const void* mask, const lkl_problem* p, const float* dloss,

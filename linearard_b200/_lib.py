@@ -30,7 +30,7 @@ MASK_DTYPES = {"bool": LKL_MASK_BOOL, "uint8": LKL_MASK_U8, "int32": LKL_MASK_I3
 EXPORTS = ("lkl_abi_version", "lkl_status_string", "lkl_workspace_size", "lkl_lse",
            "lkl_kl_forward", "lkl_forward", "lkl_backward", "lkl_device_status",
            "lkl_last_path", "lkl_set_force_generic", "lkl_forward_noalloc",
-           "lkl_last_cuda_error")
+           "lkl_last_cuda_error", "lkl_backward_workspace_size")
 
 
 class LKLProblem(ctypes.Structure):
@@ -65,6 +65,8 @@ def _declare(L):
     L.lkl_status_string.argtypes = [_i32]
     L.lkl_workspace_size.restype = _sz
     L.lkl_workspace_size.argtypes = [_P, _i32]
+    L.lkl_backward_workspace_size.restype = _sz
+    L.lkl_backward_workspace_size.argtypes = [_P, _i32]
     L.lkl_lse.restype = _i32
     L.lkl_lse.argtypes = [_vp, _vp, _vp, _P, _vp, _vp, _sz, _vp]
     L.lkl_kl_forward.restype = _i32

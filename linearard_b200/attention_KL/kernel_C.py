@@ -42,7 +42,7 @@ def kl_backward(qs, ks, lse_s, qt, kt, lse_t, attn_mask=None, causal=True,
     dk = dq if fused else torch.empty((B, ks.shape[1], T, Ds), device=qs.device,
                                       dtype=torch.float32)
     with torch.cuda.device(qs.device):
-        ws, n = workspace(prob, mask is not None, qs.device)
+        ws, n = workspace(prob, mask is not None, qs.device, backward=True)
         st = _lib.lib().lkl_backward(ptr(qs), ptr(ks), ptr(lse_s), ptr(qt), ptr(kt), ptr(lse_t),
                                      ptr(mask), ctypes.byref(prob), ptr(dloss), ptr(dq), ptr(dk),
                                      ptr(ws), n, stream_of(qs.device))

@@ -180,6 +180,12 @@ size_t lkl_workspace_size(const lkl_problem* p, int32_t has_mask) {
   return n;
 }
 
+size_t lkl_backward_workspace_size(const lkl_problem* p, int32_t has_mask) {
+  const size_t base = lkl_workspace_size(p, has_mask);
+  if (base == 0 || check_problem(p, true) != LKL_OK) return base;
+  return base + round256(lkl::sm100_dbuf_bytes(to_problem(p)));
+}
+
 int32_t lkl_lse(const void* q, const void* k, const void* mask, const lkl_problem* p, float* lse,
                 void* ws, size_t ws_bytes, void* stream) {
   int32_t s = check_problem(p, false);
@@ -276,6 +282,7 @@ int32_t lkl_backward(const void* qs, const void* ks, const float* lse_s, const v
   if (alias && (qs != ks || p->Hkv_s != p->Hq)) return LKL_ERR_BAD_ALIAS;
   if (p->B == 0 || p->T == 0) return LKL_OK;
   if ((s = check_workspace(p, mask, ws, ws_bytes))) return s;
+  if (ws_bytes < lkl_backward_workspace_size(p, mask != nullptr)) return LKL_ERR_WORKSPACE;
   if (!bind_device_of(qs) || !device_is_sm100()) return LKL_ERR_NO_DEVICE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint32_t* bits;
@@ -283,10 +290,12 @@ int32_t lkl_backward(const void* qs, const void* ks, const float* lse_s, const v
   const Problem q = to_problem(p);
   cudaError_t e;
   if (use_tensor_cores(q, qs, ks, qt, kt) && lkl::sm100_backward_supports(q)) {
-    // every gradient row is written by exactly one CTA: no clearing needed
+    // every gradient row is written by exactly one CTA per chunk: no clearing needed
     t_last_path = 1;
+    const size_t base = lkl_workspace_size(p, mask != nullptr);
     e = lkl::launch_sm100_backward(q, qs, ks, lse_s, qt, kt, lse_t, bits, dloss, dq, dk, alias,
-                                   lsc_ptr(p, mask, ws), st);
+                                   lsc_ptr(p, mask, ws), static_cast<uint8_t*>(ws) + base,
+                                   ws_bytes - base, st);
   } else {
     // dk (and dq when it is the same buffer) accumulates with atomics
     const size_t dk_bytes = (size_t)p->B * p->Hkv_s * p->T * p->Ds * sizeof(float);

@@ -87,13 +87,17 @@ cudaError_t launch_sm100_forward(const Problem& p, const void* qs, const void* k
                                  const void* qt, const void* kt, const uint32_t* bits,
                                  float* lse_s, float* lse_t, float* partials,
                                  int* num_partials, cudaStream_t st);
-// Backward (dq then dk, no reductions); needs Hkv_s == Hkv_t.  `lsc` is
-// B*Hq*T float2 of scratch for the per-row exponent offsets.
+// Backward: per chunk, a dq launch that also stores the rounded D tiles into
+// `dbuf`, then a dk GEMM launch over them; no reductions.  Needs Hkv_s ==
+// Hkv_t.  `lsc` is B*Hq*T float2 of scratch, `dbuf` at least
+// sm100_dbuf_bytes(p) bytes (smaller buffers give more, smaller chunks; too
+// small for one query-tile row of a kv group -> cudaErrorInvalidValue).
 bool sm100_backward_supports(const Problem& p);
+size_t sm100_dbuf_bytes(const Problem& p);
 cudaError_t launch_sm100_backward(const Problem& p, const void* qs, const void* ks,
                                   const float* lse_s, const void* qt, const void* kt,
                                   const float* lse_t, const uint32_t* bits, const float* dloss,
-                                  float* dq, float* dk, bool alias, float2* lsc,
-                                  cudaStream_t st);
+                                  float* dq, float* dk, bool alias, float2* lsc, void* dbuf,
+                                  size_t dbuf_bytes, cudaStream_t st);
 
 }  // namespace lkl

@@ -26,7 +26,9 @@
 // columns), warp 16 = TMA producer, warp 17 = MMA issuer and TMEM owner.
 #include <math_constants.h>
 
+#include <algorithm>
 #include <mutex>
+#include <vector>
 
 #include "lkl_common.cuh"
 #include "sm100_ptx.cuh"
@@ -49,6 +51,8 @@ constexpr int kThreads = 32 * (kRowWarps + 2);
 constexpr int kMaxDynSmem = 232448;
 constexpr int kMisc = 1024;
 constexpr uint32_t kTmemCols = 512;
+// Upper bound of the D buffer (the backward's bf16/fp16 D tiles of one chunk).
+constexpr long long kDBufCapBytes = 8ll << 30;
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -515,14 +519,35 @@ __device__ __forceinline__ void tile_row_to_tmem(const uint8_t* tile, int r, uin
   }
 }
 
-template <int DS, int DT, bool DK, bool BF16>
+// One backward chunk: kv groups [bk0, bk0 + nk) (query heads bk0*G ..), query
+// tiles [i0, i1) of each; their D tiles are stored in the D buffer,
+// head-major, row tile by row tile (tiles j <= i per row when causal).
+struct Chunk {
+  int bk0, nk, i0, i1;
+  int dq_acc;            // dq adds into the output (alias, non-causal, split rows)
+  long long tph;         // D tiles per query head in this chunk
+};
+
+__host__ __device__ __forceinline__ long long d_row_offset(const Problem& p, const Chunk& c,
+                                                           int i, int n_t) {
+  return p.causal ? ((long long)i * (i + 1) / 2 - (long long)c.i0 * (c.i0 + 1) / 2)
+                  : (long long)(i - c.i0) * n_t;
+}
+
+constexpr int kDTileElems = kBM * kBN;  // one D tile: [128 query rows][128 key columns]
+
+// dq launch: one CTA per (query head, query tile i).  Recomputes both score
+// tiles against every key tile j, forms D = e^{ss - lse_s} - e^{st - lse_t}
+// (masked, rounded to the input dtype), accumulates dq_i += D Ks_j in TMEM and
+// stores D to the D buffer for the dk launch.
+template <int DS, int DT, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
-sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
-                  const __grid_constant__ CUtensorMap tm_ks,
-                  const __grid_constant__ CUtensorMap tm_qt,
-                  const __grid_constant__ CUtensorMap tm_kt, const Problem p,
-                  const float2* __restrict__ lsc, const uint32_t* __restrict__ bits,
-                  const float* __restrict__ dloss, float* out, int accumulate) {
+sm100_dq_kernel(const __grid_constant__ CUtensorMap tm_qs,
+                const __grid_constant__ CUtensorMap tm_ks,
+                const __grid_constant__ CUtensorMap tm_qt,
+                const __grid_constant__ CUtensorMap tm_kt, const Problem p, const Chunk c,
+                const float2* __restrict__ lsc, const uint32_t* __restrict__ bits,
+                const float* __restrict__ dloss, float* out, uint16_t* __restrict__ dbuf) {
   using L = GradLayout<DS, DT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -538,30 +563,16 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
 
   // ---- work of this CTA (head-major, longest first)
   const int n_t = (p.T + kBM - 1) / kBM;
-  int b, hs, ht, st_tile, n_steps, n_per_head, first_tile, bh0;
-  if (DK) {
-    const int G = p.Hq / p.Hkv_s;
-    const int bk = (int)(blockIdx.x / n_t);
-    st_tile = (int)(blockIdx.x % n_t);  // key tile, ascending = longest first
-    b = bk / p.Hkv_s;
-    hs = bk % p.Hkv_s;
-    ht = hs;  // the tensor-core dk path requires Hkv_s == Hkv_t
-    first_tile = p.causal ? st_tile : 0;
-    n_per_head = n_t - first_tile;
-    n_steps = G * n_per_head;
-    bh0 = b * p.Hq + hs * G;
-  } else {
-    const int bh = (int)(blockIdx.x / n_t);
-    st_tile = n_t - 1 - (int)(blockIdx.x % n_t);  // query tile, descending = longest first
-    b = bh / p.Hq;
-    const int h = bh % p.Hq;
-    hs = h / (p.Hq / p.Hkv_s);
-    ht = h / (p.Hq / p.Hkv_t);
-    first_tile = 0;
-    n_per_head = p.causal ? st_tile + 1 : n_t;
-    n_steps = n_per_head;
-    bh0 = bh;
-  }
+  const int G = p.Hq / p.Hkv_s;
+  const int n_i = c.i1 - c.i0;
+  const int local = (int)(blockIdx.x / n_i);
+  const int st_tile = c.i1 - 1 - (int)(blockIdx.x % n_i);  // descending = longest first
+  const int bh = c.bk0 * G + local;
+  const int b = bh / p.Hq, h = bh % p.Hq;
+  const int hs = h / G, ht = h / (p.Hq / p.Hkv_t);
+  const int n_steps = p.causal ? st_tile + 1 : n_t;
+  uint16_t* const drow = dbuf + ((long long)local * c.tph + d_row_offset(p, c, st_tile, n_t)) *
+                                    (long long)kDTileElems;
 
   if (warp == kProducerWarp && lane == 0) {
     tma_prefetch_desc(&tm_qs);
@@ -576,13 +587,8 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
     if (lane == 0) {
       // ---------------- TMA producer
       mbar_arrive_expect_tx(&misc->q_full, L::QS + L::QT);
-      if (DK) {
-        issue_tile_loads(smem + L::OFF_QS, &tm_ks, &misc->q_full, DS, st_tile * kBM, b * p.Hkv_s + hs);
-        issue_tile_loads(smem + L::OFF_QT, &tm_kt, &misc->q_full, DT, st_tile * kBM, b * p.Hkv_t + ht);
-      } else {
-        issue_tile_loads(smem + L::OFF_QS, &tm_qs, &misc->q_full, DS, st_tile * kBM, bh0);
-        issue_tile_loads(smem + L::OFF_QT, &tm_qt, &misc->q_full, DT, st_tile * kBM, bh0);
-      }
+      issue_tile_loads(smem + L::OFF_QS, &tm_qs, &misc->q_full, DS, st_tile * kBM, bh);
+      issue_tile_loads(smem + L::OFF_QT, &tm_qt, &misc->q_full, DT, st_tile * kBM, bh);
       for (int j = 0; j < n_steps; ++j) {
         const int s = j % L::NS;
         if (j >= L::NS && !mbar_wait(&misc->k_empty[s], ((j / L::NS) - 1) & 1, abort, err)) break;
@@ -590,16 +596,9 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
         if (j == L::NS - 1 && !mbar_wait(&misc->a_ready, 0, abort, err)) break;
         uint8_t* stg = smem + L::OFF_K + s * L::STAGE;
         mbar_arrive_expect_tx(&misc->k_full[s], L::STAGE);
-        const int tile = first_tile + j % n_per_head;
-        if (DK) {
-          const int bh = bh0 + j / n_per_head;
-          issue_tile_loads(stg, &tm_qs, &misc->k_full[s], DS, tile * kBN, bh);
-          issue_tile_loads(stg + kBN * DS * 2, &tm_qt, &misc->k_full[s], DT, tile * kBN, bh);
-        } else {
-          issue_tile_loads(stg, &tm_ks, &misc->k_full[s], DS, tile * kBN, b * p.Hkv_s + hs);
-          issue_tile_loads(stg + kBN * DS * 2, &tm_kt, &misc->k_full[s], DT, tile * kBN,
-                           b * p.Hkv_t + ht);
-        }
+        issue_tile_loads(stg, &tm_ks, &misc->k_full[s], DS, j * kBN, b * p.Hkv_s + hs);
+        issue_tile_loads(stg + kBN * DS * 2, &tm_kt, &misc->k_full[s], DT, j * kBN,
+                         b * p.Hkv_t + ht);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -654,20 +653,15 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
     const int wg = warp >> 2, q = warp & 3;
     const int r = q * 32 + lane;
     const int words = (p.T + 31) >> 5;
-    const int own = st_tile * kBM + r;  // query row (dq) or key row (dk) of this lane
+    const int own = st_tile * kBM + r;  // query row of this lane
     const bool own_in = own < p.T;
     const float cs = p.sc_s * kLog2e, ct = p.sc_t * kLog2e;
     const float gscale = p.sc_s * (dloss ? *dloss : 1.f);
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
-    // dq: this row's exponent offsets; dk: whether this key takes part at all
+    // this row's exponent offsets (-inf for rows that take no gradient)
     float2 Lrow = make_float2(-CUDART_INF_F, -CUDART_INF_F);
-    bool key_ok = true;
-    if (!DK) {
-      if (own_in) Lrow = lsc[(size_t)bh0 * p.T + own];
-    } else {
-      key_ok = own_in && token_valid(bits, words, b, own);
-    }
-    const bool row_live = DK ? key_ok : (Lrow.x != -CUDART_INF_F);
+    if (own_in) Lrow = lsc[(size_t)bh * p.T + own];
+    const bool row_live = Lrow.x != -CUDART_INF_F;
     if (wg == 0) {
       // warpgroup 0 moves the stationary tiles (all 128 rows) into TMEM
       if (mbar_wait(&misc->q_full, 0, abort, err)) {
@@ -680,17 +674,13 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
     }
     const uint64_t cs2 = f2pack(cs, cs), ct2 = f2pack(ct, ct);
     const uint64_t nls2 = f2pack(Lrow.x, Lrow.x), nlt2 = f2pack(Lrow.y, Lrow.y);
+    // D tiles are stored as 16 groups of 8 key columns, each [128 query rows]
+    // x 16 bytes (the no-swizzle core-matrix layout the dk GEMM reads): this
+    // thread's 32 columns are groups 4 wg .. 4 wg + 3 of row r, so a warp's
+    // store covers 512 contiguous bytes
+    uint4* dst = reinterpret_cast<uint4*>(drow) + (wg * 4) * kBM + r;
 
     for (int j = 0; j < n_steps; ++j) {
-      const int tile = first_tile + j % n_per_head;
-      // dk: lane k fetches the exponent offsets of columns k and 32 + k of this
-      // warpgroup's 64 query rows before the scores arrive; they are handed to
-      // the other lanes with shuffles
-      float2 lA = make_float2(0.f, 0.f);
-      if (DK) {
-        const float2* lcol = lsc + (size_t)(bh0 + j / n_per_head) * p.T;
-        lA = lcol[min(tile * kBN + wg * 32 + lane, p.T - 1)];
-      }
       if (!mbar_wait(&misc->s_full[0], j & 1, abort, err)) break;
       tc_fence_after();
       uint32_t packed[16];
@@ -706,40 +696,22 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
       __syncwarp();
       if (lane == 0) mbar_arrive(&misc->s_empty[0]);
       {
-        const int c0 = tile * kBN + wg * 32;  // first streamed row of these columns
-        // (no early exit for dead rows: the dk branch shuffles across the warp)
+        const int c0 = j * kBN + wg * 32;  // first key column of this thread
         float d[32];
 #pragma unroll
         for (int k = 0; k < 32; k += 2) {
-          uint64_t nl_s = nls2, nl_t = nlt2;
-          if (DK) {
-            nl_s = f2pack(__shfl_sync(0xffffffffu, lA.x, k), __shfl_sync(0xffffffffu, lA.x, k + 1));
-            nl_t = f2pack(__shfl_sync(0xffffffffu, lA.y, k), __shfl_sync(0xffffffffu, lA.y, k + 1));
-          }
           float a0, a1, b0, b1;
-          f2unpack(ffma2(f2pack(x[k], x[k + 1]), cs2, nl_s), a0, a1);
-          f2unpack(ffma2(f2pack(y[k], y[k + 1]), ct2, nl_t), b0, b1);
+          f2unpack(ffma2(f2pack(x[k], x[k + 1]), cs2, nls2), a0, a1);
+          f2unpack(ffma2(f2pack(y[k], y[k + 1]), ct2, nlt2), b0, b1);
           f2unpack(fsub2(f2pack(ex2(a0), ex2(a1)), f2pack(ex2(b0), ex2(b1))), d[k], d[k + 1]);
         }
-        bool full;
-        if (!DK) {
-          // columns are keys c: valid iff c <= i (causal), c < T, key not padded
-          const int lim = p.causal ? min(own, p.T - 1) : p.T - 1;
-          full = (c0 + 31 <= lim) && (bits == nullptr);
-          if (!full) {
+        // columns are keys c: valid iff c <= i (causal), c < T, key not padded
+        const int lim = p.causal ? min(own, p.T - 1) : p.T - 1;
+        const bool full = (c0 + 31 <= lim) && (bits == nullptr);
+        if (!full) {
 #pragma unroll
-            for (int k = 0; k < 32; ++k)
-              if (!((c0 + k <= lim) && token_valid(bits, words, b, c0 + k))) d[k] = 0.f;
-          }
-        } else {
-          // columns are query rows c: valid iff c >= j (causal) and c < T; padded
-          // or LSE-less rows carry -inf offsets and give 0 by themselves
-          full = (!p.causal || c0 >= own) && (c0 + 31 < p.T);
-          if (!full) {
-#pragma unroll
-            for (int k = 0; k < 32; ++k)
-              if (!((c0 + k < p.T) && (!p.causal || c0 + k >= own))) d[k] = 0.f;
-          }
+          for (int k = 0; k < 32; ++k)
+            if (!((c0 + k <= lim) && token_valid(bits, words, b, c0 + k))) d[k] = 0.f;
         }
         if (!row_live) {
 #pragma unroll
@@ -748,6 +720,12 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
 #pragma unroll
         for (int k = 0; k < 32; k += 2) packed[k >> 1] = pack2t<BF16>(d[k], d[k + 1]);
       }
+      // D to the buffer read by the dk launch (64 contiguous bytes per thread)
+      uint4* dj = dst + (size_t)j * (kDTileElems / 8);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        dj[k * kBM] =
+            make_uint4(packed[4 * k], packed[4 * k + 1], packed[4 * k + 2], packed[4 * k + 3]);
       if (j > 0) {
         if (!mbar_wait(&misc->d_empty, (j - 1) & 1, abort, err)) break;
         tc_fence_after();
@@ -761,10 +739,9 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
     }
     if (n_steps > 0 && mbar_wait(&misc->d_empty, (n_steps - 1) & 1, abort, err)) {
       tc_fence_after();
-      float* row = DK ? out + (((size_t)b * p.Hkv_s + hs) * p.T + own) * DS
-                      : out + ((size_t)bh0 * p.T + own) * DS;
+      float* row = out + ((size_t)bh * p.T + own) * DS;
       store_rows<DS / 4>(lane_addr + kColAcc + wg * (DS / 4), row + wg * (DS / 4), gscale, own_in,
-                     DK && accumulate != 0);
+                         c.dq_acc != 0);
     }
   }
 
@@ -773,6 +750,131 @@ sm100_grad_kernel(const __grid_constant__ CUtensorMap tm_qs,
   if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// dk launch: a plain pipelined GEMM.  One CTA per (kv head, key tile j):
+// dk_j = sum over the group's query heads and query tiles i of D_ij^T Qs_i,
+// both operands MN-major in shared memory (D: one bulk copy of a tile stored
+// in the no-swizzle core-matrix layout; Qs: TMA, 128-byte swizzle), the
+// accumulator in TMEM.  Warp 0 = TMA producer, warp 1 =
+// MMA issuer and TMEM owner, warps 2-5 = epilogue (TMEM lanes 32 (w % 4)).
+constexpr int kDkThreads = 192;
+constexpr uint32_t kDkTmemCols = 128;
+
+template <int DS>
+struct DkLayout {
+  static constexpr int DT_BYTES = kDTileElems * 2, Q_BYTES = kBM * DS * 2;
+  static constexpr int STAGE = DT_BYTES + Q_BYTES;
+  static constexpr int AVAIL = kMaxDynSmem - 1024 - kMisc;
+  static constexpr int NS = (AVAIL / STAGE) >= 4 ? 4 : (AVAIL / STAGE);
+  static constexpr int OFF_MISC = NS * STAGE;
+  static constexpr int BYTES = 1024 + OFF_MISC + kMisc;
+  static_assert(NS >= 2, "dk GEMM needs two stages");
+};
+
+template <int DS>
+__global__ void __launch_bounds__(kDkThreads, 1)
+sm100_dk_kernel(const __grid_constant__ CUtensorMap tm_qs, const Problem p, const Chunk c,
+                const uint16_t* __restrict__ dbuf, const float* __restrict__ dloss, float* out,
+                int alias) {
+  using L = DkLayout<DS>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  Misc* misc = reinterpret_cast<Misc*>(smem + L::OFF_MISC);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* err = &g_device_error;
+  volatile int* abort = &misc->abort;
+
+  const int n_t = (p.T + kBM - 1) / kBM;
+  const int G = p.Hq / p.Hkv_s;
+  const int n_j = p.causal ? c.i1 : n_t;  // key tiles that meet this chunk's query tiles
+  const int lk = (int)(blockIdx.x / n_j);
+  const int j = (int)(blockIdx.x % n_j);  // ascending = longest first
+  const int bk = c.bk0 + lk;
+  const int i_first = p.causal ? max(c.i0, j) : c.i0;
+  const int n_i = c.i1 - i_first;
+  const int n_steps = G * n_i;
+  // the first chunk that reaches key tile j stores, later ones add
+  const bool accumulate = alias != 0 || (p.causal ? j < c.i0 : c.i0 > 0);
+
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_qs);
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < 4; ++s) {
+      mbar_init(&misc->k_full[s], 1);
+      mbar_init(&misc->k_empty[s], 1);
+    }
+    mbar_init(&misc->d_full, 1);
+    misc->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&misc->tmem_base, kDkTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = misc->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int s = 0; s < n_steps; ++s) {
+        const int slot = s % L::NS;
+        if (s >= L::NS && !mbar_wait(&misc->k_empty[slot], ((s / L::NS) - 1) & 1, abort, err))
+          break;
+        const int g = s / n_i, i = i_first + s % n_i;
+        const long long tile =
+            (long long)(lk * G + g) * c.tph + d_row_offset(p, c, i, n_t) + j;
+        uint8_t* stg = smem + slot * L::STAGE;
+        mbar_arrive_expect_tx(&misc->k_full[slot], L::STAGE);
+        bulk_load(stg, dbuf + tile * kDTileElems, L::DT_BYTES, &misc->k_full[slot]);
+        issue_tile_loads(stg + L::DT_BYTES, &tm_qs, &misc->k_full[slot], DS, i * kBM,
+                         bk * G + g);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // acc[key j][feature] += sum over query rows of D[query][key] Qs[query][feature]:
+      // A = D^T and B = Qs, both MN-major in shared memory
+      const uint32_t id = idesc_f16(kBN, DS, p.dtype_s, p.dtype_s, 1, 1);
+      bool ok = true;
+      for (int s = 0; s < n_steps; ++s) {
+        const int slot = s % L::NS;
+        if (!mbar_wait(&misc->k_full[slot], (s / L::NS) & 1, abort, err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a = smem_u32(smem + slot * L::STAGE), bq = a + L::DT_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < kBM / 16; ++kk)
+          umma_f16_ss(tmem, desc_interleave(a + kk * 2 * 128, 128, kBM * 16),
+                      mnmajor_desc(bq, kk), id,
+                      (s > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&misc->k_empty[slot]);
+      }
+      if (ok) umma_commit(&misc->d_full);
+    }
+  } else {
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int own = j * kBN + r;  // key row of this lane
+    const float gscale = p.sc_s * (dloss ? *dloss : 1.f);
+    if (n_steps > 0 && mbar_wait(&misc->d_full, 0, abort, err)) {
+      tc_fence_after();
+      float* row = out + ((size_t)bk * p.T + own) * DS;
+      store_rows<DS>(tmem + ((uint32_t)(q * 32) << 16), row, gscale, own < p.T, accumulate);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kDkTmemCols);
   }
 }
 
@@ -842,32 +944,99 @@ cudaError_t run_forward(const Problem& p, const Maps& m, const uint32_t* bits, f
 }
 
 template <int DS, int DT>
-cudaError_t run_grad(const Problem& p, const Maps& m, const float2* lsc, const uint32_t* bits,
-                     const float* dloss, float* dq, float* dk, bool alias, cudaStream_t st) {
+cudaError_t run_grad(const Problem& p, const Maps& m, const std::vector<Chunk>& plan, const float2* lsc, const uint32_t* bits,
+                     const float* dloss, float* dq, float* dk, bool alias, uint16_t* dbuf,
+                     cudaStream_t st) {
   using L = GradLayout<DS, DT>;
+  using LK = DkLayout<DS>;
   const bool bf = p.dtype_s == LKL_BF16;
-  auto kq = bf ? sm100_grad_kernel<DS, DT, false, true> : sm100_grad_kernel<DS, DT, false, false>;
-  auto kk = bf ? sm100_grad_kernel<DS, DT, true, true> : sm100_grad_kernel<DS, DT, true, false>;
+  auto kq = bf ? sm100_dq_kernel<DS, DT, true> : sm100_dq_kernel<DS, DT, false>;
+  auto kk = sm100_dk_kernel<DS>;
   cudaError_t e = prep(kq, L::BYTES);
-  if (e == cudaSuccess) e = prep(kk, L::BYTES);
+  if (e == cudaSuccess) e = prep(kk, LK::BYTES);
   if (e != cudaSuccess) return e;
   const int n_t = (p.T + kBM - 1) / kBM;
-  // dq first (plain stores); then dk, which in the fused case adds into the same rows
-  kq<<<p.B * p.Hq * n_t, kThreads, L::BYTES, st>>>(m.qs, m.ks, m.qt, m.kt, p, lsc, bits, dloss,
-                                                    dq, 0);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  kk<<<p.B * p.Hkv_s * n_t, kThreads, L::BYTES, st>>>(m.qs, m.ks, m.qt, m.kt, p, lsc, bits,
-                                                       dloss, alias ? dq : dk, alias ? 1 : 0);
-  return cudaGetLastError();
+  const int G = p.Hq / p.Hkv_s;
+  for (const Chunk& c : plan) {
+    // dq rows of the chunk (stores D); then dk, which in the fused case adds
+    // into rows that dq has already written
+    kq<<<c.nk * G * (c.i1 - c.i0), kThreads, L::BYTES, st>>>(m.qs, m.ks, m.qt, m.kt, p, c, lsc,
+                                                             bits, dloss, dq, dbuf);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const int n_j = p.causal ? c.i1 : n_t;
+    kk<<<c.nk * n_j, kDkThreads, LK::BYTES, st>>>(m.qs, p, c, dbuf, dloss, alias ? dq : dk,
+                                                   alias ? 1 : 0);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+constexpr long long kDTileBytes = (long long)kDTileElems * 2;
+
+long long d_tiles_per_head(const Problem& p) {
+  const long long n_t = (p.T + kBM - 1) / kBM;
+  return p.causal ? n_t * (n_t + 1) / 2 : n_t * n_t;
+}
+
+// Splits the backward into chunks whose D tiles fit `cap_tiles`: whole kv
+// groups when one group fits, otherwise one group at a time in ranges of
+// query tiles.  Returns false when not even one query-tile row of a group fits.
+bool plan_chunks(const Problem& p, long long cap_tiles, bool alias, std::vector<Chunk>& out,
+                 bool& zero_dq) {
+  const int n_t = (p.T + kBM - 1) / kBM;
+  const int G = p.Hq / p.Hkv_s;
+  const int groups = p.B * p.Hkv_s;
+  const long long group_tiles = (long long)G * d_tiles_per_head(p);
+  out.clear();
+  zero_dq = false;
+  if (group_tiles <= cap_tiles) {
+    const int per = (int)std::min<long long>(groups, cap_tiles / group_tiles);
+    for (int g0 = 0; g0 < groups; g0 += per) {
+      Chunk c{};
+      c.bk0 = g0;
+      c.nk = std::min(per, groups - g0);
+      c.i0 = 0;
+      c.i1 = n_t;
+      c.tph = d_tiles_per_head(p);
+      out.push_back(c);
+    }
+    return true;
+  }
+  const bool acc = alias && !p.causal;
+  for (int g0 = 0; g0 < groups; ++g0) {
+    for (int i0 = 0; i0 < n_t;) {
+      long long tiles = 0;
+      int i1 = i0;
+      for (; i1 < n_t; ++i1) {
+        const long long row_tiles = p.causal ? i1 + 1 : n_t;
+        if ((long long)G * (tiles + row_tiles) > cap_tiles) break;
+        tiles += row_tiles;
+      }
+      if (i1 == i0) return false;
+      Chunk c{};
+      c.bk0 = g0;
+      c.nk = 1;
+      c.i0 = i0;
+      c.i1 = i1;
+      c.tph = tiles;
+      c.dq_acc = acc ? 1 : 0;
+      out.push_back(c);
+      i0 = i1;
+    }
+  }
+  zero_dq = acc;
+  return true;
 }
 
 }  // namespace
 
-bool sm100_supports(const Problem& p) {
+bool sm100_shape_ok(const Problem& p) {
   const bool ds_ok = p.Ds == 64 || p.Ds == 128;
   const bool dt_ok = p.Dt == 64 || p.Dt == 128;
-  return ds_ok && dt_ok && p.sc_s > 0.f && p.sc_t > 0.f && p.T >= 1 && get_encoder() != nullptr;
+  return ds_ok && dt_ok && p.sc_s > 0.f && p.sc_t > 0.f && p.T >= 1;
 }
+
+bool sm100_supports(const Problem& p) { return sm100_shape_ok(p) && get_encoder() != nullptr; }
 
 int sm100_num_partials(const Problem& p) { return p.B * p.Hq * ((p.T + kBM - 1) / kBM); }
 
@@ -888,11 +1057,23 @@ bool sm100_backward_supports(const Problem& p) {
   return sm100_supports(p) && p.Hkv_s == p.Hkv_t;
 }
 
+size_t sm100_dbuf_bytes(const Problem& p) {
+  if (p.B <= 0 || p.T <= 0 || !sm100_shape_ok(p) || p.Hkv_s != p.Hkv_t) return 0;
+  const long long all = (long long)p.B * p.Hq * d_tiles_per_head(p);
+  const long long cap = kDBufCapBytes / kDTileBytes;
+  const long long row = (long long)(p.Hq / p.Hkv_s) * ((p.T + kBM - 1) / kBM);
+  return (size_t)(std::max(std::min(all, cap), row) * kDTileBytes);
+}
+
 cudaError_t launch_sm100_backward(const Problem& p, const void* qs, const void* ks,
                                   const float* lse_s, const void* qt, const void* kt,
                                   const float* lse_t, const uint32_t* bits, const float* dloss,
-                                  float* dq, float* dk, bool alias, float2* lsc,
-                                  cudaStream_t st) {
+                                  float* dq, float* dk, bool alias, float2* lsc, void* dbuf,
+                                  size_t dbuf_bytes, cudaStream_t st) {
+  std::vector<Chunk> plan;
+  bool zero_dq = false;
+  const long long cap_tiles = (long long)(dbuf_bytes / kDTileBytes);
+  if (!plan_chunks(p, cap_tiles, alias, plan, zero_dq)) return cudaErrorInvalidValue;
   Maps m;
   if (!build_maps(m, p, qs, ks, qt, kt)) return cudaErrorInvalidValue;
   const size_t rows = (size_t)p.B * p.Hq * p.T;
@@ -900,10 +1081,16 @@ cudaError_t launch_sm100_backward(const Problem& p, const void* qs, const void* 
   scale_lse_kernel<<<grid, 256, 0, st>>>(lse_s, lse_t, bits, p.B, p.Hq, p.T, lsc);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  if (p.Ds == 128 && p.Dt == 128) return run_grad<128, 128>(p, m, lsc, bits, dloss, dq, dk, alias, st);
-  if (p.Ds == 64 && p.Dt == 64) return run_grad<64, 64>(p, m, lsc, bits, dloss, dq, dk, alias, st);
-  if (p.Ds == 128 && p.Dt == 64) return run_grad<128, 64>(p, m, lsc, bits, dloss, dq, dk, alias, st);
-  return run_grad<64, 128>(p, m, lsc, bits, dloss, dq, dk, alias, st);
+  if (zero_dq && (e = cudaMemsetAsync(dq, 0, rows * p.Ds * sizeof(float), st)) != cudaSuccess)
+    return e;
+  uint16_t* d16 = static_cast<uint16_t*>(dbuf);
+  if (p.Ds == 128 && p.Dt == 128)
+    return run_grad<128, 128>(p, m, plan, lsc, bits, dloss, dq, dk, alias, d16, st);
+  if (p.Ds == 64 && p.Dt == 64)
+    return run_grad<64, 64>(p, m, plan, lsc, bits, dloss, dq, dk, alias, d16, st);
+  if (p.Ds == 128 && p.Dt == 64)
+    return run_grad<128, 64>(p, m, plan, lsc, bits, dloss, dq, dk, alias, d16, st);
+  return run_grad<64, 128>(p, m, plan, lsc, bits, dloss, dq, dk, alias, d16, st);
 }
 
 }  // namespace lkl

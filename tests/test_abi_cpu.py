@@ -27,7 +27,7 @@ def test_library_loads_and_exports_header_symbols():
     assert set(names) == set(_lib.EXPORTS)
     for n in names:
         assert hasattr(L, n), n
-    assert L.lkl_abi_version() == 1
+    assert L.lkl_abi_version() == 2
 
 
 def test_status_strings():
@@ -54,6 +54,42 @@ def test_workspace_size():
     assert n0 >= 4 * 1 * 4 * ((300 + 31) // 32)
     assert n1 - n0 >= 1 * ((300 + 31) // 32) * 4
     assert L.lkl_workspace_size(ctypes.byref(_prob(T=0)), 1) == 0
+
+
+def test_backward_workspace_holds_the_d_tiles():
+    """Tensor-core shapes add one 32 KB D tile per (query head, tile pair);
+    beyond 8 GiB the buffer is capped and the backward runs in chunks."""
+    L = _lib.lib()
+    for mask in (0, 1):
+        p = _prob(Hkv_t=2)                      # Hkv_s == Hkv_t: tensor-core backward
+        base = L.lkl_workspace_size(ctypes.byref(p), mask)
+        n_t = (300 + 127) // 128
+        tiles = 1 * 4 * n_t * (n_t + 1) // 2    # causal: tiles j <= i per head
+        assert L.lkl_backward_workspace_size(ctypes.byref(p), mask) == base + tiles * 32768
+        nc = _prob(Hkv_t=2, causal=0)
+        assert (L.lkl_backward_workspace_size(ctypes.byref(nc), mask)
+                == L.lkl_workspace_size(ctypes.byref(nc), mask) + 4 * n_t * n_t * 32768)
+    # shapes served by the CUDA-core kernels need nothing extra
+    for kw in (dict(), dict(Ds=32, Dt=32, Hkv_t=2)):   # Hkv_s != Hkv_t; head dim 32
+        p = _prob(**kw)
+        assert (L.lkl_backward_workspace_size(ctypes.byref(p), 0)
+                == L.lkl_workspace_size(ctypes.byref(p), 0))
+    # LLaMA3-8B Q/Q relation at 32K: 32 heads x 32896 tiles -> capped at 8 GiB
+    big = _prob(B=1, Hq=32, Hkv_s=32, Hkv_t=32, T=32768)
+    extra = (L.lkl_backward_workspace_size(ctypes.byref(big), 0)
+             - L.lkl_workspace_size(ctypes.byref(big), 0))
+    assert extra == 8 << 30
+    assert L.lkl_backward_workspace_size(ctypes.byref(_prob(T=0)), 0) == 0
+
+
+def test_backward_rejects_a_forward_sized_workspace():
+    L = _lib.lib()
+    p = _prob(Hkv_t=2)
+    fake = ctypes.c_void_p(0x10000)
+    n = L.lkl_workspace_size(ctypes.byref(p), 0)
+    st = L.lkl_backward(fake, fake, fake, fake, fake, fake, None, ctypes.byref(p), None,
+                        fake, ctypes.c_void_p(0x20000), fake, n, None)
+    assert st == 6, _lib.STATUS.get(st)
 
 
 @pytest.mark.parametrize("kw,code", [
