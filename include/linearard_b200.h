@@ -130,8 +130,11 @@ int32_t lkl_forward(const void* qs, const void* ks, const void* qt, const void* 
  * dq + dk, the gradient of the shared tensor.
  * Replaces kl_backward_triton (kernels/attention_KL/kernel_C.py:293-449) and
  * the chain rule in AttnKLAlignFn.backward (integration.py:48-67).
- * The workspace must hold lkl_backward_workspace_size(p, mask != NULL) bytes
- * (LKL_ERR_WORKSPACE otherwise). */
+ * Workspace: lkl_backward_workspace_size(p, mask != NULL) bytes give the
+ * fastest plan.  Less also works, down to lkl_workspace_size plus one
+ * query-tile row of D tiles of one kv group ((Hq / Hkv_s) * ceil(T / 128)
+ * tiles of 32 KB) for the tensor-core shapes, in more and smaller chunks;
+ * below that LKL_ERR_WORKSPACE. */
 int32_t lkl_backward(const void* qs, const void* ks, const float* lse_s,
                      const void* qt, const void* kt, const float* lse_t,
                      const void* mask, const lkl_problem* p, const float* dloss,

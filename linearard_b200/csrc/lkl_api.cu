@@ -282,7 +282,10 @@ int32_t lkl_backward(const void* qs, const void* ks, const float* lse_s, const v
   if (alias && (qs != ks || p->Hkv_s != p->Hq)) return LKL_ERR_BAD_ALIAS;
   if (p->B == 0 || p->T == 0) return LKL_OK;
   if ((s = check_workspace(p, mask, ws, ws_bytes))) return s;
-  if (ws_bytes < lkl_backward_workspace_size(p, mask != nullptr)) return LKL_ERR_WORKSPACE;
+  // the tensor-core backward needs room for at least one chunk of D tiles
+  // beyond the common scratch; more room means fewer, larger chunks
+  const size_t base = lkl_workspace_size(p, mask != nullptr);
+  if (ws_bytes < base + lkl::sm100_dbuf_min_bytes(to_problem(p))) return LKL_ERR_WORKSPACE;
   if (!bind_device_of(qs) || !device_is_sm100()) return LKL_ERR_NO_DEVICE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint32_t* bits;
@@ -292,7 +295,6 @@ int32_t lkl_backward(const void* qs, const void* ks, const float* lse_s, const v
   if (use_tensor_cores(q, qs, ks, qt, kt) && lkl::sm100_backward_supports(q)) {
     // every gradient row is written by exactly one CTA per chunk: no clearing needed
     t_last_path = 1;
-    const size_t base = lkl_workspace_size(p, mask != nullptr);
     e = lkl::launch_sm100_backward(q, qs, ks, lse_s, qt, kt, lse_t, bits, dloss, dq, dk, alias,
                                    lsc_ptr(p, mask, ws), static_cast<uint8_t*>(ws) + base,
                                    ws_bytes - base, st);

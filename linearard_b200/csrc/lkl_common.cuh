@@ -94,6 +94,8 @@ cudaError_t launch_sm100_forward(const Problem& p, const void* qs, const void* k
 // small for one query-tile row of a kv group -> cudaErrorInvalidValue).
 bool sm100_backward_supports(const Problem& p);
 size_t sm100_dbuf_bytes(const Problem& p);
+// Smallest D buffer the backward runs with (one query-tile row of a kv group).
+size_t sm100_dbuf_min_bytes(const Problem& p);
 cudaError_t launch_sm100_backward(const Problem& p, const void* qs, const void* ks,
                                   const float* lse_s, const void* qt, const void* kt,
                                   const float* lse_t, const uint32_t* bits, const float* dloss,

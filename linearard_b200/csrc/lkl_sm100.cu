@@ -753,14 +753,16 @@ sm100_dq_kernel(const __grid_constant__ CUtensorMap tm_qs,
   }
 }
 
-// dk launch: a plain pipelined GEMM.  One CTA per (kv head, key tile j):
-// dk_j = sum over the group's query heads and query tiles i of D_ij^T Qs_i,
-// both operands MN-major in shared memory (D: one bulk copy of a tile stored
-// in the no-swizzle core-matrix layout; Qs: TMA, 128-byte swizzle), the
-// accumulator in TMEM.  Warp 0 = TMA producer, warp 1 =
-// MMA issuer and TMEM owner, warps 2-5 = epilogue (TMEM lanes 32 (w % 4)).
+// dk launch: a plain pipelined GEMM, persistent.  Work item = (kv head, key
+// tile j): dk_j = sum over the group's query heads and query tiles i of
+// D_ij^T Qs_i, both operands MN-major in shared memory (D: one bulk copy of a
+// tile stored in the no-swizzle core-matrix layout; Qs: TMA, 128-byte
+// swizzle), the accumulator in TMEM (two buffers, so that the epilogue of one
+// item overlaps the GEMM of the next).  One CTA per SM; HBM-bound.
+// Warp 0 = TMA producer, warp 1 = MMA issuer and TMEM owner, warps 2-5 =
+// epilogue (TMEM lanes 32 (w % 4)).
 constexpr int kDkThreads = 192;
-constexpr uint32_t kDkTmemCols = 128;
+constexpr uint32_t kDkTmemCols = 256;
 
 template <int DS>
 struct DkLayout {
@@ -772,6 +774,11 @@ struct DkLayout {
   static constexpr int BYTES = 1024 + OFF_MISC + kMisc;
   static_assert(NS >= 2, "dk GEMM needs two stages");
 };
+
+// Items of one dk launch per kv head: the key tiles that meet the chunk's query tiles.
+__host__ __device__ __forceinline__ int dk_tiles_per_head(const Problem& p, const Chunk& c) {
+  return p.causal ? c.i1 : (p.T + kBM - 1) / kBM;
+}
 
 template <int DS>
 __global__ void __launch_bounds__(kDkThreads, 1)
@@ -788,25 +795,33 @@ sm100_dk_kernel(const __grid_constant__ CUtensorMap tm_qs, const Problem p, cons
 
   const int n_t = (p.T + kBM - 1) / kBM;
   const int G = p.Hq / p.Hkv_s;
-  const int n_j = p.causal ? c.i1 : n_t;  // key tiles that meet this chunk's query tiles
-  const int lk = (int)(blockIdx.x / n_j);
-  const int j = (int)(blockIdx.x % n_j);  // ascending = longest first
-  const int bk = c.bk0 + lk;
-  const int i_first = p.causal ? max(c.i0, j) : c.i0;
-  const int n_i = c.i1 - i_first;
-  const int n_steps = G * n_i;
-  // the first chunk that reaches key tile j stores, later ones add
-  const bool accumulate = alias != 0 || (p.causal ? j < c.i0 : c.i0 > 0);
+  const int n_j = dk_tiles_per_head(p, c);
+  const int n_items = c.nk * n_j;
+  // Round rd of this CTA takes item rd * grid + b, or rd * grid + grid - 1 - b
+  // in odd rounds ("snake" order).  Items are key-tile major (j ascending =
+  // longest first when causal), so the snake evens out the CTAs' work.
+  auto item_at = [&](int rd) {
+    const int g = (int)gridDim.x, b = (int)blockIdx.x;
+    return rd * g + ((rd & 1) ? g - 1 - b : b);
+  };
+  // item -> (kv head of the chunk, key tile, first query tile, query tiles)
+  auto item_of = [&](int item, int& lk, int& j, int& i_first, int& n_i) {
+    j = item / c.nk;
+    lk = item % c.nk;
+    i_first = p.causal ? max(c.i0, j) : c.i0;
+    n_i = c.i1 - i_first;
+  };
 
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tm_qs);
-  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tm_qs);
   if (threadIdx.x == 0) {
     for (int s = 0; s < 4; ++s) {
       mbar_init(&misc->k_full[s], 1);
       mbar_init(&misc->k_empty[s], 1);
     }
-    mbar_init(&misc->d_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&misc->s_full[b], 1);   // accumulator b complete
+      mbar_init(&misc->s_empty[b], 4);  // accumulator b drained by the epilogue warps
+    }
     misc->abort = 0;
     fence_barrier_init();
   }
@@ -821,52 +836,81 @@ sm100_dk_kernel(const __grid_constant__ CUtensorMap tm_qs, const Problem p, cons
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int s = 0; s < n_steps; ++s) {
-        const int slot = s % L::NS;
-        if (s >= L::NS && !mbar_wait(&misc->k_empty[slot], ((s / L::NS) - 1) & 1, abort, err))
-          break;
-        const int g = s / n_i, i = i_first + s % n_i;
-        const long long tile =
-            (long long)(lk * G + g) * c.tph + d_row_offset(p, c, i, n_t) + j;
-        uint8_t* stg = smem + slot * L::STAGE;
-        mbar_arrive_expect_tx(&misc->k_full[slot], L::STAGE);
-        bulk_load(stg, dbuf + tile * kDTileElems, L::DT_BYTES, &misc->k_full[slot]);
-        issue_tile_loads(stg + L::DT_BYTES, &tm_qs, &misc->k_full[slot], DS, i * kBM,
-                         bk * G + g);
+      int gs = 0;  // running stage counter over all items of this CTA
+      bool ok = true;
+      for (int rd = 0, item = item_at(0); ok && item < n_items; item = item_at(++rd)) {
+        int lk, j, i_first, n_i;
+        item_of(item, lk, j, i_first, n_i);
+        const int bk = c.bk0 + lk;
+        for (int s = 0; s < G * n_i; ++s, ++gs) {
+          const int slot = gs % L::NS;
+          if (gs >= L::NS &&
+              !mbar_wait(&misc->k_empty[slot], ((gs / L::NS) - 1) & 1, abort, err)) {
+            ok = false;
+            break;
+          }
+          const int g = s / n_i, i = i_first + s % n_i;
+          const long long tile =
+              (long long)(lk * G + g) * c.tph + d_row_offset(p, c, i, n_t) + j;
+          uint8_t* stg = smem + slot * L::STAGE;
+          mbar_arrive_expect_tx(&misc->k_full[slot], L::STAGE);
+          bulk_load(stg, dbuf + tile * kDTileElems, L::DT_BYTES, &misc->k_full[slot]);
+          issue_tile_loads(stg + L::DT_BYTES, &tm_qs, &misc->k_full[slot], DS, i * kBM,
+                           bk * G + g);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // acc[key j][feature] += sum over query rows of D[query][key] Qs[query][feature]:
-      // A = D^T and B = Qs, both MN-major in shared memory
+      // A = D^T (no swizzle, MN-major) and B = Qs (128B swizzle, MN-major)
       const uint32_t id = idesc_f16(kBN, DS, p.dtype_s, p.dtype_s, 1, 1);
+      int gs = 0, it = 0;
       bool ok = true;
-      for (int s = 0; s < n_steps; ++s) {
-        const int slot = s % L::NS;
-        if (!mbar_wait(&misc->k_full[slot], (s / L::NS) & 1, abort, err)) {
-          ok = false;
-          break;
-        }
+      for (int rd = 0, item = item_at(0); ok && item < n_items; item = item_at(++rd), ++it) {
+        int lk, j, i_first, n_i;
+        item_of(item, lk, j, i_first, n_i);
+        const int ab = it & 1;
+        if (it >= 2 && !mbar_wait(&misc->s_empty[ab], ((it >> 1) - 1) & 1, abort, err)) break;
         tc_fence_after();
-        const uint32_t a = smem_u32(smem + slot * L::STAGE), bq = a + L::DT_BYTES;
+        const uint32_t acc = tmem + ab * 128;
+        for (int s = 0; s < G * n_i; ++s, ++gs) {
+          const int slot = gs % L::NS;
+          if (!mbar_wait(&misc->k_full[slot], (gs / L::NS) & 1, abort, err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(smem + slot * L::STAGE), bq = a + L::DT_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < kBM / 16; ++kk)
-          umma_f16_ss(tmem, desc_interleave(a + kk * 2 * 128, 128, kBM * 16),
-                      mnmajor_desc(bq, kk), id,
-                      (s > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&misc->k_empty[slot]);
+          for (int kk = 0; kk < kBM / 16; ++kk)
+            umma_f16_ss(acc, desc_interleave(a + kk * 2 * 128, 128, kBM * 16),
+                        mnmajor_desc(bq, kk), id, (s > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&misc->k_empty[slot]);
+        }
+        if (ok) umma_commit(&misc->s_full[ab]);
       }
-      if (ok) umma_commit(&misc->d_full);
     }
   } else {
     const int q = warp & 3;
     const int r = q * 32 + lane;
-    const int own = j * kBN + r;  // key row of this lane
     const float gscale = p.sc_s * (dloss ? *dloss : 1.f);
-    if (n_steps > 0 && mbar_wait(&misc->d_full, 0, abort, err)) {
+    int it = 0;
+    for (int rd = 0, item = item_at(0); item < n_items; item = item_at(++rd), ++it) {
+      int lk, j, i_first, n_i;
+      item_of(item, lk, j, i_first, n_i);
+      const int ab = it & 1;
+      if (!mbar_wait(&misc->s_full[ab], (it >> 1) & 1, abort, err)) break;
       tc_fence_after();
-      float* row = out + ((size_t)bk * p.T + own) * DS;
-      store_rows<DS>(tmem + ((uint32_t)(q * 32) << 16), row, gscale, own < p.T, accumulate);
+      const int own = j * kBN + r;  // key row of this lane
+      // the first chunk that reaches key tile j stores, later ones add
+      const bool accumulate = alias != 0 || (p.causal ? j < c.i0 : c.i0 > 0);
+      float* row = out + ((size_t)(c.bk0 + lk) * p.T + own) * DS;
+      store_rows<DS>(tmem + ab * 128 + ((uint32_t)(q * 32) << 16), row, gscale, own < p.T,
+                     accumulate);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&misc->s_empty[ab]);
     }
   }
 
@@ -944,9 +988,9 @@ cudaError_t run_forward(const Problem& p, const Maps& m, const uint32_t* bits, f
 }
 
 template <int DS, int DT>
-cudaError_t run_grad(const Problem& p, const Maps& m, const std::vector<Chunk>& plan, const float2* lsc, const uint32_t* bits,
-                     const float* dloss, float* dq, float* dk, bool alias, uint16_t* dbuf,
-                     cudaStream_t st) {
+cudaError_t run_grad(const Problem& p, const Maps& m, const std::vector<Chunk>& plan,
+                     const float2* lsc, const uint32_t* bits, const float* dloss, float* dq,
+                     float* dk, bool alias, uint16_t* dbuf, cudaStream_t st) {
   using L = GradLayout<DS, DT>;
   using LK = DkLayout<DS>;
   const bool bf = p.dtype_s == LKL_BF16;
@@ -955,17 +999,22 @@ cudaError_t run_grad(const Problem& p, const Maps& m, const std::vector<Chunk>& 
   cudaError_t e = prep(kq, L::BYTES);
   if (e == cudaSuccess) e = prep(kk, LK::BYTES);
   if (e != cudaSuccess) return e;
-  const int n_t = (p.T + kBM - 1) / kBM;
+  int dev = 0, num_sms = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess ||
+      (e = cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+    return e;
   const int G = p.Hq / p.Hkv_s;
   for (const Chunk& c : plan) {
     // dq rows of the chunk (stores D); then dk, which in the fused case adds
-    // into rows that dq has already written
+    // into rows that dq has already written.  (Running the HBM-bound dk
+    // launch beside the next chunk's dq launch was measured: no gain, the
+    // chip is at its power limit either way.)
     kq<<<c.nk * G * (c.i1 - c.i0), kThreads, L::BYTES, st>>>(m.qs, m.ks, m.qt, m.kt, p, c, lsc,
                                                              bits, dloss, dq, dbuf);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    const int n_j = p.causal ? c.i1 : n_t;
-    kk<<<c.nk * n_j, kDkThreads, LK::BYTES, st>>>(m.qs, p, c, dbuf, dloss, alias ? dq : dk,
-                                                   alias ? 1 : 0);
+    const int grid = std::min(c.nk * dk_tiles_per_head(p, c), num_sms);
+    kk<<<grid, kDkThreads, LK::BYTES, st>>>(m.qs, p, c, dbuf, dloss, alias ? dq : dk,
+                                            alias ? 1 : 0);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -990,11 +1039,14 @@ bool plan_chunks(const Problem& p, long long cap_tiles, bool alias, std::vector<
   out.clear();
   zero_dq = false;
   if (group_tiles <= cap_tiles) {
+    // as few chunks as fit, of near-equal size (a small last chunk would
+    // leave most SMs idle)
     const int per = (int)std::min<long long>(groups, cap_tiles / group_tiles);
-    for (int g0 = 0; g0 < groups; g0 += per) {
+    const int n_chunks = (groups + per - 1) / per;
+    for (int k = 0; k < n_chunks; ++k) {
       Chunk c{};
-      c.bk0 = g0;
-      c.nk = std::min(per, groups - g0);
+      c.bk0 = (int)((long long)k * groups / n_chunks);
+      c.nk = (int)((long long)(k + 1) * groups / n_chunks) - c.bk0;
       c.i0 = 0;
       c.i1 = n_t;
       c.tph = d_tiles_per_head(p);
@@ -1065,6 +1117,11 @@ size_t sm100_dbuf_bytes(const Problem& p) {
   return (size_t)(std::max(std::min(all, cap), row) * kDTileBytes);
 }
 
+size_t sm100_dbuf_min_bytes(const Problem& p) {
+  if (sm100_dbuf_bytes(p) == 0) return 0;
+  return (size_t)((long long)(p.Hq / p.Hkv_s) * ((p.T + kBM - 1) / kBM) * kDTileBytes);
+}
+
 cudaError_t launch_sm100_backward(const Problem& p, const void* qs, const void* ks,
                                   const float* lse_s, const void* qt, const void* kt,
                                   const float* lse_t, const uint32_t* bits, const float* dloss,
@@ -1072,8 +1129,8 @@ cudaError_t launch_sm100_backward(const Problem& p, const void* qs, const void* 
                                   size_t dbuf_bytes, cudaStream_t st) {
   std::vector<Chunk> plan;
   bool zero_dq = false;
-  const long long cap_tiles = (long long)(dbuf_bytes / kDTileBytes);
-  if (!plan_chunks(p, cap_tiles, alias, plan, zero_dq)) return cudaErrorInvalidValue;
+  if (!plan_chunks(p, (long long)(dbuf_bytes / kDTileBytes), alias, plan, zero_dq))
+    return cudaErrorInvalidValue;
   Maps m;
   if (!build_maps(m, p, qs, ks, qt, kt)) return cudaErrorInvalidValue;
   const size_t rows = (size_t)p.B * p.Hq * p.T;
