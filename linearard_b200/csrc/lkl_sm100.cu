@@ -13,15 +13,16 @@
 //   A = sum_j e^{st_j - m_t} (st_j - ss_j), so that
 //   KL_i = A / l_t + lse_s - lse_t   (exact: sum_j pt_j = 1).
 //
-// Backward (replaces kernel_C, kernel_C.py:63-261):
-//   recompute ss, st; D = e^{ss - lse_s} - e^{st - lse_t} rounded to the input
-//   dtype and written to shared memory in the UMMA K-major 128B-swizzled
-//   layout; then dq_i += D Ks_j (TMEM accumulator for the whole row tile) and
-//   dk_part = D^T Qs_i (same shared buffer read as MN-major; for d = 128 its
-//   transpose Qs_i^T D, so that TMEM lanes are features), the latter drained
-//   by the row warps with fp32 reductions into dk.
+// Backward (replaces kernel_C, kernel_C.py:63-261), per chunk of the D-tile
+// buffer, two launches and no reductions:
+//   dq launch (row-stationary, same shape as the forward): recompute ss, st;
+//   D = e^{ss - lse_s} - e^{st - lse_t} rounded to the input dtype (as
+//   kernel_C.py:233), written to TMEM as the A operand of dq_i += D Ks_j and
+//   to the D buffer in HBM (no-swizzle core-matrix layout, 32 KB per tile);
+//   dk launch (persistent GEMM): dk_j = sum_i D_ij^T Qs_i, streaming D back.
+// Every gradient row is written by one CTA per chunk: bit-reproducible.
 //
-// Warp roles (576 threads): warps 0-15 = row warps in four warpgroups (warp
+// Warp roles of the forward and dq kernels (576 threads): warps 0-15 = row warps in four warpgroups (warp
 // w reads TMEM lanes 32*(w%4) .. +31; warpgroup g owns 32 of each tile's 128
 // columns), warp 16 = TMA producer, warp 17 = MMA issuer and TMEM owner.
 #include <math_constants.h>

@@ -12,8 +12,10 @@ import csv
 import io
 import sys
 
-SHORT = (("sm100_backward_kernel", "sm100_backward_kernel"),
+SHORT = (("sm100_dq_kernel", "sm100_dq_kernel"),
+         ("sm100_dk_kernel", "sm100_dk_kernel"),
          ("sm100_forward_kernel", "sm100_forward_kernel"),
+         ("scale_lse_kernel", "scale_lse_kernel"),
          ("generic_backward_kernel", "generic_backward_kernel"),
          ("generic_forward_kernel", "generic_forward_kernel"),
          ("reduce_partials_kernel", "reduce_partials_kernel"),
@@ -46,17 +48,23 @@ def _rows(path):
     return list(csv.reader(io.StringIO(text[start:])))
 
 
+_TIME_NS = {"nsecond": 1.0, "ns": 1.0, "usecond": 1e3, "us": 1e3, "msecond": 1e6, "ms": 1e6,
+            "second": 1e9, "s": 1e9}
+
+
 def launches(path):
     rows = _rows(path)
     hdr = rows[0]
     ki, vi, mi = hdr.index("Kernel Name"), hdr.index("Metric Value"), hdr.index("Metric Name")
+    ui = hdr.index("Metric Unit") if "Metric Unit" in hdr else None
     agg = collections.OrderedDict()
     for r in rows[1:]:
         if len(r) < len(hdr) or r[mi] != "gpu__time_duration.sum":
             continue
         a = agg.setdefault(short_name(r[ki]), [0, 0.0])
         a[0] += 1
-        a[1] += float(r[vi].replace(",", ""))
+        scale = _TIME_NS.get(r[ui], 1.0) if ui is not None else 1.0
+        a[1] += float(r[vi].replace(",", "")) * scale
     tot = sum(v[1] for v in agg.values())
     print(f"{'kernel':58s} {'launches':>8s} {'total ms':>10s} {'share':>7s}")
     for k, (n, t) in sorted(agg.items(), key=lambda x: -x[1][1]):
@@ -67,6 +75,7 @@ def launches(path):
 def raw(path):
     rows = _rows(path)
     hdr = rows[0]
+    units = rows[1] if len(rows) > 1 and not rows[1][0].strip().isdigit() else [""] * len(hdr)
     ki = hdr.index("Kernel Name")
     for r in rows[1:]:
         if len(r) < len(hdr) or not r[0].strip().isdigit():
@@ -74,7 +83,8 @@ def raw(path):
         print(f"== {short_name(r[ki])} (ID {r[0]})")
         for key in RAW_KEYS:
             if key in hdr:
-                print(f"   {key:70s} {r[hdr.index(key)]}")
+                i = hdr.index(key)
+                print(f"   {key:70s} {r[i]:>14s} {units[i]}")
 
 
 if __name__ == "__main__":
