@@ -26,6 +26,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+E2E_SLICE = 8      # heads per host->device slice in the end-to-end measurement
 METRIC = "KL fwd+bwd tokens/s, LLaMA3-8B heads @32K ctx; % bf16 tensor peak"
 WORKLOAD = "llama3_8b_32k"
 
@@ -334,19 +335,44 @@ def main():
     # ---- end to end from pinned host buffers through the public API
     e2e = None
     if not args.no_e2e:
-        host_s = {r: v.detach().cpu().pin_memory() for r, v in students.items()}
-        host_t = {r: v.cpu().pin_memory() for r, v in teachers.items()}
-        dev_s = {r: torch.empty_like(v) for r, v in students.items()}
-        dev_t = {r: torch.empty_like(v) for r, v in teachers.items()}
-        h2d = sum(v.numel() * v.element_size() for v in host_s.values()) + \
-            sum(v.numel() * v.element_size() for v in host_t.values())
+        # The inputs of each relation arrive from pinned host memory in slices of
+        # E2E_SLICE heads, each its own leaf tensor and its own attn_kl_align call
+        # (the loss is a sum over heads).  All copies go out on a copy stream at
+        # the start of the step; the forward of slice k waits only for slice k's
+        # copy, so the PCIe transfer of later slices runs under earlier compute.
+        slices = []
+        for r in cfg.relations:
+            H = students[r].shape[1]
+            for h0 in range(0, H, E2E_SLICE):
+                h1 = min(H, h0 + E2E_SLICE)
+                hs = students[r].detach()[:, h0:h1].contiguous().cpu().pin_memory()
+                ht = teachers[r][:, h0:h1].contiguous().cpu().pin_memory()
+                slices.append((hs, ht, torch.empty_like(hs, device=dev),
+                               torch.empty_like(ht, device=dev)))
+        h2d = sum(x.numel() * x.element_size() for sl in slices for x in sl[:2])
+        copy_stream = torch.cuda.Stream(device=dev)
+        copied = [torch.cuda.Event() for _ in slices]
 
         def e2e_step():
-            for r in cfg.relations:
-                dev_s[r].copy_(host_s[r], non_blocking=True)
-                dev_t[r].copy_(host_t[r], non_blocking=True)
-            S = {r: dev_s[r].detach().requires_grad_(True) for r in cfg.relations}
-            return float(step(S, dev_t).item())   # device -> host read of the loss
+            cur = torch.cuda.current_stream(dev)
+            copy_stream.wait_stream(cur)   # the previous step is done with the buffers
+            with torch.cuda.stream(copy_stream):
+                for (hs, ht, ds, dt), ev in zip(slices, copied):
+                    ds.copy_(hs, non_blocking=True)
+                    dt.copy_(ht, non_blocking=True)
+                    ev.record(copy_stream)
+            total = None
+            for (_, _, ds, dt), ev in zip(slices, copied):
+                cur.wait_event(ev)
+                s_leaf = ds.detach().requires_grad_(True)
+                l = attn_kl_align(s_leaf, s_leaf, dt, dt, None, cfg.causal)
+                total = l if total is None else total + l
+            total.backward()
+            if world > 1:
+                red = total.detach().clone()
+                dist.all_reduce(red)
+                total = red
+            return float(total.item())   # device -> host read of the loss
 
         for _ in range(max(1, args.warmup)):
             e2e_step()
