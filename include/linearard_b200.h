@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define LKL_ABI_VERSION 2
+#define LKL_ABI_VERSION 3
 
 /* element types of q/k tensors */
 enum lkl_dtype { LKL_F16 = 0, LKL_BF16 = 1 };
@@ -64,7 +64,9 @@ enum lkl_status {
   LKL_ERR_NO_DEVICE = 8,        /* current device is not sm_100 / no CUDA device     */
   LKL_ERR_DEVICE_TIMEOUT = 9,   /* a device-side bounded wait expired (see below)    */
   LKL_ERR_BAD_ALIAS = 10,       /* dq == dk requires qs == ks and Hkv_s == Hq        */
-  LKL_ERR_TOO_LARGE = 11        /* a size exceeds what the entry point supports      */
+  LKL_ERR_TOO_LARGE = 11,       /* a size exceeds what the entry point supports      */
+  LKL_ERR_UNSUPPORTED = 12      /* strided inputs on a shape the tensor-core path
+                                   does not cover (ABI version 3)                     */
 };
 
 /* Shape / option block shared by every entry point. */
@@ -140,6 +142,34 @@ int32_t lkl_backward(const void* qs, const void* ks, const float* lse_s,
                      const void* mask, const lkl_problem* p, const float* dloss,
                      float* dq, float* dk, void* workspace, size_t workspace_bytes,
                      void* stream);
+
+/* ---- Strided inputs (ABI version 3) ----
+ * The hot-path entry points above take contiguous [B, H, T, D] tensors, as the
+ * reference wrappers require (kernel_B.py:289-290).  These two take each of
+ * qs, ks, qt, kt as a [B, H, T, D] view with element strides (b, h, t) and a
+ * d stride of 1, e.g. the transposed [B, T, H, D] projections that an
+ * attention hook sees before it calls .contiguous() (train.py:133-142).  The
+ * tensors are read in place through TMA, so no copy is made.
+ * Requirements: every stride a positive multiple of 8 elements and every base
+ * pointer 16-byte aligned (LKL_ERR_MISALIGNED otherwise); the tensor-core path
+ * (sm_100, Ds and Dt in {64, 128}, and Hkv_s == Hkv_t for the backward),
+ * LKL_ERR_UNSUPPORTED otherwise.  Outputs (lse, loss, dq, dk) are contiguous,
+ * as in lkl_forward / lkl_backward; everything else is the same.
+ * `strides` points to 4 entries: qs, ks, qt, kt. */
+typedef struct lkl_strides {
+  int64_t b, h, t;    /* element strides of the batch, head and token dims */
+} lkl_strides;
+
+int32_t lkl_forward_strided(const void* qs, const void* ks, const void* qt, const void* kt,
+                            const lkl_strides* strides, const void* mask,
+                            const lkl_problem* p, float* lse_s, float* lse_t, float* loss,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+int32_t lkl_backward_strided(const void* qs, const void* ks, const float* lse_s,
+                             const void* qt, const void* kt, const float* lse_t,
+                             const lkl_strides* strides, const void* mask,
+                             const lkl_problem* p, const float* dloss, float* dq, float* dk,
+                             void* workspace, size_t workspace_bytes, void* stream);
 
 /* Device-side error word of the current device: the bounded waits inside the
  * tensor-core kernels set it instead of hanging.  Reads (synchronously) and

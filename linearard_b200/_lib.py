@@ -12,7 +12,7 @@ import threading
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "liblinearard_b200.so")
 
-__all__ = ["LKLProblem", "lib", "check", "LKLError",
+__all__ = ["LKLProblem", "LKLStrides", "lib", "check", "LKLError",
            "LKL_F16", "LKL_BF16", "MASK_DTYPES", "STATUS"]
 
 LKL_F16, LKL_BF16 = 0, 1
@@ -21,7 +21,7 @@ STATUS = {
     0: "LKL_OK", 1: "LKL_ERR_NULL_POINTER", 2: "LKL_ERR_BAD_SHAPE", 3: "LKL_ERR_BAD_HEAD_DIM",
     4: "LKL_ERR_BAD_DTYPE", 5: "LKL_ERR_MISALIGNED", 6: "LKL_ERR_WORKSPACE", 7: "LKL_ERR_LAUNCH",
     8: "LKL_ERR_NO_DEVICE", 9: "LKL_ERR_DEVICE_TIMEOUT", 10: "LKL_ERR_BAD_ALIAS",
-    11: "LKL_ERR_TOO_LARGE",
+    11: "LKL_ERR_TOO_LARGE", 12: "LKL_ERR_UNSUPPORTED",
 }
 MASK_DTYPES = {"bool": LKL_MASK_BOOL, "uint8": LKL_MASK_U8, "int32": LKL_MASK_I32,
                "int64": LKL_MASK_I64}
@@ -30,7 +30,8 @@ MASK_DTYPES = {"bool": LKL_MASK_BOOL, "uint8": LKL_MASK_U8, "int32": LKL_MASK_I3
 EXPORTS = ("lkl_abi_version", "lkl_status_string", "lkl_workspace_size", "lkl_lse",
            "lkl_kl_forward", "lkl_forward", "lkl_backward", "lkl_device_status",
            "lkl_last_path", "lkl_set_force_generic", "lkl_forward_noalloc",
-           "lkl_last_cuda_error", "lkl_backward_workspace_size")
+           "lkl_last_cuda_error", "lkl_backward_workspace_size", "lkl_forward_strided",
+           "lkl_backward_strided")
 
 
 class LKLProblem(ctypes.Structure):
@@ -41,6 +42,11 @@ class LKLProblem(ctypes.Structure):
         ("causal", ctypes.c_int32), ("mask_dtype", ctypes.c_int32),
         ("sm_scale_s", ctypes.c_float), ("sm_scale_t", ctypes.c_float),
     ]
+
+
+class LKLStrides(ctypes.Structure):
+    """Element strides (b, h, t) of a [B, H, T, D] input whose d stride is 1."""
+    _fields_ = [("b", ctypes.c_int64), ("h", ctypes.c_int64), ("t", ctypes.c_int64)]
 
 
 class LKLError(RuntimeError):
@@ -80,6 +86,13 @@ def _declare(L):
     L.lkl_last_cuda_error.restype = _i32
     L.lkl_set_force_generic.restype = None
     L.lkl_set_force_generic.argtypes = [_i32]
+    _S = ctypes.POINTER(LKLStrides)
+    L.lkl_forward_strided.restype = _i32
+    L.lkl_forward_strided.argtypes = [_vp, _vp, _vp, _vp, _S, _vp, _P, _vp, _vp, _vp, _vp, _sz,
+                                      _vp]
+    L.lkl_backward_strided.restype = _i32
+    L.lkl_backward_strided.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _S, _vp, _P, _vp, _vp, _vp,
+                                       _vp, _sz, _vp]
     L.lkl_forward_noalloc.restype = _i32
     L.lkl_forward_noalloc.argtypes = [_vp, _vp, _vp, _vp, _vp, _P, _vp, _vp, _vp, _vp]
 

@@ -167,6 +167,9 @@ const char* lkl_status_string(int32_t s) {
     case LKL_ERR_DEVICE_TIMEOUT: return "a device-side bounded wait expired";
     case LKL_ERR_BAD_ALIAS: return "dq == dk requires qs == ks and Hkv_s == Hq";
     case LKL_ERR_TOO_LARGE: return "problem exceeds the supported size";
+    case LKL_ERR_UNSUPPORTED:
+      return "strided inputs need the tensor-core path (sm_100, Ds and Dt in {64, 128}, "
+             "16-byte aligned; Hkv_s == Hkv_t for the backward)";
     default: return "unknown status";
   }
 }
@@ -235,9 +238,30 @@ int32_t lkl_kl_forward(const void* qs, const void* ks, const float* lse_s, const
   return launch_status(lkl::launch_reduce_partials(part, np, loss, st));
 }
 
-int32_t lkl_forward(const void* qs, const void* ks, const void* qt, const void* kt,
-                    const void* mask, const lkl_problem* p, float* lse_s, float* lse_t,
-                    float* loss, void* ws, size_t ws_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Strided inputs: every stride a positive multiple of 8 elements (16 bytes,
+// the TMA rule), base pointers 16-byte aligned.
+int32_t check_strides(const lkl_strides* s, const void* const ptrs[4]) {
+  if (!s) return LKL_ERR_NULL_POINTER;
+  for (int i = 0; i < 4; ++i) {
+    if (s[i].b <= 0 || s[i].h <= 0 || s[i].t <= 0) return LKL_ERR_BAD_SHAPE;
+    if (s[i].b % 8 || s[i].h % 8 || s[i].t % 8 || !aligned(ptrs[i], 16)) return LKL_ERR_MISALIGNED;
+  }
+  return LKL_OK;
+}
+
+void to_strides(const lkl_strides* s, lkl::TensorStrides out[4]) {
+  for (int i = 0; i < 4; ++i) out[i] = lkl::TensorStrides{s[i].b, s[i].h, s[i].t};
+}
+
+// lkl_forward with optional strides (nullptr = contiguous inputs).
+int32_t forward_impl(const void* qs, const void* ks, const void* qt, const void* kt,
+                     const lkl_strides* strides, const void* mask, const lkl_problem* p,
+                     float* lse_s, float* lse_t, float* loss, void* ws, size_t ws_bytes,
+                     void* stream) {
   int32_t s = check_problem(p, true);
   if (s) return s;
   if (!qs || !ks || !qt || !kt || !lse_s || !lse_t || !loss) return LKL_ERR_NULL_POINTER;
@@ -245,19 +269,26 @@ int32_t lkl_forward(const void* qs, const void* ks, const void* qt, const void* 
       !aligned(lse_s, 4) || !aligned(lse_t, 4) || !aligned(loss, 4))
     return LKL_ERR_MISALIGNED;
   if ((s = check_mask(mask, p->mask_dtype))) return s;
+  const void* const ptrs[4] = {qs, ks, qt, kt};
+  if (strides && (s = check_strides(strides, ptrs))) return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (p->B == 0 || p->T == 0) return launch_status(cudaMemsetAsync(loss, 0, sizeof(float), st));
   if ((s = check_workspace(p, mask, ws, ws_bytes))) return s;
   if (!bind_device_of(qs) || !device_is_sm100()) return LKL_ERR_NO_DEVICE;
+  const Problem q = to_problem(p);
+  const bool tc = use_tensor_cores(q, qs, ks, qt, kt);
+  if (strides && !tc) return LKL_ERR_UNSUPPORTED;
   uint32_t* bits;
   if ((s = prepare_mask(p, mask, ws, &bits, st))) return s;
-  const Problem q = to_problem(p);
   float* part = partials_ptr(p, mask, ws);
   int np = 0;
   cudaError_t e;
-  if (use_tensor_cores(q, qs, ks, qt, kt)) {
+  if (tc) {
     t_last_path = 1;
-    e = lkl::launch_sm100_forward(q, qs, ks, qt, kt, bits, lse_s, lse_t, part, &np, st);
+    lkl::TensorStrides ts[4];
+    if (strides) to_strides(strides, ts);
+    e = lkl::launch_sm100_forward(q, qs, ks, qt, kt, strides ? ts : nullptr, bits, lse_s, lse_t,
+                                  part, &np, st);
   } else {
     t_last_path = 0;
     e = lkl::launch_generic_forward(1, q, qs, ks, qt, kt, bits, lse_s, lse_t, part, &np, st);
@@ -266,10 +297,11 @@ int32_t lkl_forward(const void* qs, const void* ks, const void* qt, const void* 
   return launch_status(lkl::launch_reduce_partials(part, np, loss, st));
 }
 
-int32_t lkl_backward(const void* qs, const void* ks, const float* lse_s, const void* qt,
-                     const void* kt, const float* lse_t, const void* mask, const lkl_problem* p,
-                     const float* dloss, float* dq, float* dk, void* ws, size_t ws_bytes,
-                     void* stream) {
+// lkl_backward with optional strides (nullptr = contiguous inputs).
+int32_t backward_impl(const void* qs, const void* ks, const float* lse_s, const void* qt,
+                      const void* kt, const float* lse_t, const lkl_strides* strides,
+                      const void* mask, const lkl_problem* p, const float* dloss, float* dq,
+                      float* dk, void* ws, size_t ws_bytes, void* stream) {
   int32_t s = check_problem(p, true);
   if (s) return s;
   if (!qs || !ks || !qt || !kt || !lse_s || !lse_t || !dq || !dk) return LKL_ERR_NULL_POINTER;
@@ -278,8 +310,13 @@ int32_t lkl_backward(const void* qs, const void* ks, const float* lse_s, const v
       (dloss && !aligned(dloss, 4)))
     return LKL_ERR_MISALIGNED;
   if ((s = check_mask(mask, p->mask_dtype))) return s;
+  const void* const ptrs[4] = {qs, ks, qt, kt};
+  if (strides && (s = check_strides(strides, ptrs))) return s;
   const bool alias = dq == dk;
   if (alias && (qs != ks || p->Hkv_s != p->Hq)) return LKL_ERR_BAD_ALIAS;
+  if (alias && strides && (strides[0].b != strides[1].b || strides[0].h != strides[1].h ||
+                           strides[0].t != strides[1].t))
+    return LKL_ERR_BAD_ALIAS;
   if (p->B == 0 || p->T == 0) return LKL_OK;
   if ((s = check_workspace(p, mask, ws, ws_bytes))) return s;
   // the tensor-core backward needs room for at least one chunk of D tiles
@@ -287,17 +324,21 @@ int32_t lkl_backward(const void* qs, const void* ks, const float* lse_s, const v
   const size_t base = lkl_workspace_size(p, mask != nullptr);
   if (ws_bytes < base + lkl::sm100_dbuf_min_bytes(to_problem(p))) return LKL_ERR_WORKSPACE;
   if (!bind_device_of(qs) || !device_is_sm100()) return LKL_ERR_NO_DEVICE;
+  const Problem q = to_problem(p);
+  const bool tc = use_tensor_cores(q, qs, ks, qt, kt) && lkl::sm100_backward_supports(q);
+  if (strides && !tc) return LKL_ERR_UNSUPPORTED;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint32_t* bits;
   if ((s = prepare_mask(p, mask, ws, &bits, st))) return s;
-  const Problem q = to_problem(p);
   cudaError_t e;
-  if (use_tensor_cores(q, qs, ks, qt, kt) && lkl::sm100_backward_supports(q)) {
+  if (tc) {
     // every gradient row is written by exactly one CTA per chunk: no clearing needed
     t_last_path = 1;
-    e = lkl::launch_sm100_backward(q, qs, ks, lse_s, qt, kt, lse_t, bits, dloss, dq, dk, alias,
-                                   lsc_ptr(p, mask, ws), static_cast<uint8_t*>(ws) + base,
-                                   ws_bytes - base, st);
+    lkl::TensorStrides ts[4];
+    if (strides) to_strides(strides, ts);
+    e = lkl::launch_sm100_backward(q, qs, ks, lse_s, qt, kt, lse_t, strides ? ts : nullptr, bits,
+                                   dloss, dq, dk, alias, lsc_ptr(p, mask, ws),
+                                   static_cast<uint8_t*>(ws) + base, ws_bytes - base, st);
   } else {
     // dk (and dq when it is the same buffer) accumulates with atomics
     const size_t dk_bytes = (size_t)p->B * p->Hkv_s * p->T * p->Ds * sizeof(float);
@@ -307,6 +348,41 @@ int32_t lkl_backward(const void* qs, const void* ks, const float* lse_s, const v
                                      st);
   }
   return launch_status(e);
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t lkl_forward(const void* qs, const void* ks, const void* qt, const void* kt,
+                    const void* mask, const lkl_problem* p, float* lse_s, float* lse_t,
+                    float* loss, void* ws, size_t ws_bytes, void* stream) {
+  return forward_impl(qs, ks, qt, kt, nullptr, mask, p, lse_s, lse_t, loss, ws, ws_bytes, stream);
+}
+
+int32_t lkl_forward_strided(const void* qs, const void* ks, const void* qt, const void* kt,
+                            const lkl_strides* strides, const void* mask, const lkl_problem* p,
+                            float* lse_s, float* lse_t, float* loss, void* ws, size_t ws_bytes,
+                            void* stream) {
+  if (!strides) return LKL_ERR_NULL_POINTER;
+  return forward_impl(qs, ks, qt, kt, strides, mask, p, lse_s, lse_t, loss, ws, ws_bytes, stream);
+}
+
+int32_t lkl_backward(const void* qs, const void* ks, const float* lse_s, const void* qt,
+                     const void* kt, const float* lse_t, const void* mask, const lkl_problem* p,
+                     const float* dloss, float* dq, float* dk, void* ws, size_t ws_bytes,
+                     void* stream) {
+  return backward_impl(qs, ks, lse_s, qt, kt, lse_t, nullptr, mask, p, dloss, dq, dk, ws,
+                       ws_bytes, stream);
+}
+
+int32_t lkl_backward_strided(const void* qs, const void* ks, const float* lse_s, const void* qt,
+                             const void* kt, const float* lse_t, const lkl_strides* strides,
+                             const void* mask, const lkl_problem* p, const float* dloss,
+                             float* dq, float* dk, void* ws, size_t ws_bytes, void* stream) {
+  if (!strides) return LKL_ERR_NULL_POINTER;
+  return backward_impl(qs, ks, lse_s, qt, kt, lse_t, strides, mask, p, dloss, dq, dk, ws,
+                       ws_bytes, stream);
 }
 
 int32_t lkl_device_status(void) {

@@ -83,10 +83,16 @@ int generic_num_partials(const Problem& p);
 // sm_100a tensor-core kernels.
 bool sm100_supports(const Problem& p);
 int sm100_num_partials(const Problem& p);
+// Element strides of a [B][H][T][D] input (the d stride is 1).
+struct TensorStrides {
+  long long b, h, t;
+};
+
+// `strides`: qs, ks, qt, kt strides, or nullptr for contiguous inputs.
 cudaError_t launch_sm100_forward(const Problem& p, const void* qs, const void* ks,
-                                 const void* qt, const void* kt, const uint32_t* bits,
-                                 float* lse_s, float* lse_t, float* partials,
-                                 int* num_partials, cudaStream_t st);
+                                 const void* qt, const void* kt, const TensorStrides* strides,
+                                 const uint32_t* bits, float* lse_s, float* lse_t,
+                                 float* partials, int* num_partials, cudaStream_t st);
 // Backward: per chunk, a dq launch that also stores the rounded D tiles into
 // `dbuf`, then a dk GEMM launch over them; no reductions.  Needs Hkv_s ==
 // Hkv_t.  `lsc` is B*Hq*T float2 of scratch, `dbuf` at least
@@ -98,8 +104,9 @@ size_t sm100_dbuf_bytes(const Problem& p);
 size_t sm100_dbuf_min_bytes(const Problem& p);
 cudaError_t launch_sm100_backward(const Problem& p, const void* qs, const void* ks,
                                   const float* lse_s, const void* qt, const void* kt,
-                                  const float* lse_t, const uint32_t* bits, const float* dloss,
-                                  float* dq, float* dk, bool alias, float2* lsc, void* dbuf,
-                                  size_t dbuf_bytes, cudaStream_t st);
+                                  const float* lse_t, const TensorStrides* strides,
+                                  const uint32_t* bits, const float* dloss, float* dq, float* dk,
+                                  bool alias, float2* lsc, void* dbuf, size_t dbuf_bytes,
+                                  cudaStream_t st);
 
 }  // namespace lkl

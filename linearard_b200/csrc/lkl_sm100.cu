@@ -154,10 +154,12 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int kk) {
   return desc_sw128(base + (uint32_t)(kk * 16 * 128), kChunk, 1024);
 }
 
+// Rows [row, row + 128) of head h, batch b of a {D, T, H, B} tensor map, as
+// D / 64 swizzled [128][64] chunks.
 __device__ __forceinline__ void issue_tile_loads(void* dst, const CUtensorMap* map,
-                                                 uint64_t* bar, int D, int row, int z) {
+                                                 uint64_t* bar, int D, int row, int h, int b) {
   for (int c = 0; c < D / 64; ++c)
-    tma_load_3d(static_cast<uint8_t*>(dst) + c * kChunk, map, bar, c * 64, row, z);
+    tma_load_4d(static_cast<uint8_t*>(dst) + c * kChunk, map, bar, c * 64, row, h, b);
 }
 
 template <typename Layout>
@@ -219,16 +221,15 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs,
     if (lane == 0) {
       // ---------------- TMA producer
       mbar_arrive_expect_tx(&misc->q_full, L::QS + L::QT);
-      issue_tile_loads(smem + L::OFF_QS, &tm_qs, &misc->q_full, DS, t.mt * kBM, t.bh);
-      issue_tile_loads(smem + L::OFF_QT, &tm_qt, &misc->q_full, DT, t.mt * kBM, t.bh);
-      const int zs = t.b * p.Hkv_s + t.hs, zt = t.b * p.Hkv_t + t.ht;
+      issue_tile_loads(smem + L::OFF_QS, &tm_qs, &misc->q_full, DS, t.mt * kBM, t.h, t.b);
+      issue_tile_loads(smem + L::OFF_QT, &tm_qt, &misc->q_full, DT, t.mt * kBM, t.h, t.b);
       for (int j = 0; j < t.n_ct; ++j) {
         const int s = j % L::NS;
         if (j >= L::NS && !mbar_wait(&misc->k_empty[s], ((j / L::NS) - 1) & 1, abort, err)) break;
         uint8_t* st = smem + L::OFF_K + s * L::STAGE;
         mbar_arrive_expect_tx(&misc->k_full[s], L::STAGE);
-        issue_tile_loads(st, &tm_ks, &misc->k_full[s], DS, j * kBN, zs);
-        issue_tile_loads(st + kBN * DS * 2, &tm_kt, &misc->k_full[s], DT, j * kBN, zt);
+        issue_tile_loads(st, &tm_ks, &misc->k_full[s], DS, j * kBN, t.hs, t.b);
+        issue_tile_loads(st + kBN * DS * 2, &tm_kt, &misc->k_full[s], DT, j * kBN, t.ht, t.b);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -588,8 +589,8 @@ sm100_dq_kernel(const __grid_constant__ CUtensorMap tm_qs,
     if (lane == 0) {
       // ---------------- TMA producer
       mbar_arrive_expect_tx(&misc->q_full, L::QS + L::QT);
-      issue_tile_loads(smem + L::OFF_QS, &tm_qs, &misc->q_full, DS, st_tile * kBM, bh);
-      issue_tile_loads(smem + L::OFF_QT, &tm_qt, &misc->q_full, DT, st_tile * kBM, bh);
+      issue_tile_loads(smem + L::OFF_QS, &tm_qs, &misc->q_full, DS, st_tile * kBM, h, b);
+      issue_tile_loads(smem + L::OFF_QT, &tm_qt, &misc->q_full, DT, st_tile * kBM, h, b);
       for (int j = 0; j < n_steps; ++j) {
         const int s = j % L::NS;
         if (j >= L::NS && !mbar_wait(&misc->k_empty[s], ((j / L::NS) - 1) & 1, abort, err)) break;
@@ -597,9 +598,8 @@ sm100_dq_kernel(const __grid_constant__ CUtensorMap tm_qs,
         if (j == L::NS - 1 && !mbar_wait(&misc->a_ready, 0, abort, err)) break;
         uint8_t* stg = smem + L::OFF_K + s * L::STAGE;
         mbar_arrive_expect_tx(&misc->k_full[s], L::STAGE);
-        issue_tile_loads(stg, &tm_ks, &misc->k_full[s], DS, j * kBN, b * p.Hkv_s + hs);
-        issue_tile_loads(stg + kBN * DS * 2, &tm_kt, &misc->k_full[s], DT, j * kBN,
-                         b * p.Hkv_t + ht);
+        issue_tile_loads(stg, &tm_ks, &misc->k_full[s], DS, j * kBN, hs, b);
+        issue_tile_loads(stg + kBN * DS * 2, &tm_kt, &misc->k_full[s], DT, j * kBN, ht, b);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -857,7 +857,7 @@ sm100_dk_kernel(const __grid_constant__ CUtensorMap tm_qs, const Problem p, cons
           mbar_arrive_expect_tx(&misc->k_full[slot], L::STAGE);
           bulk_load(stg, dbuf + tile * kDTileElems, L::DT_BYTES, &misc->k_full[slot]);
           issue_tile_loads(stg + L::DT_BYTES, &tm_qs, &misc->k_full[slot], DS, i * kBM,
-                           bk * G + g);
+                           (bk % p.Hkv_s) * G + g, bk / p.Hkv_s);
         }
       }
     }
@@ -943,17 +943,20 @@ EncodeTiledFn get_encoder() {
   return fn;
 }
 
-// [BH][T][D] 16-bit tensor viewed as a 3-D map with a {64, 128, 1} box.
-bool make_map(CUtensorMap* m, const void* ptr, int dtype, int D, int T, int BH) {
+// A [B][H][T][D] 16-bit tensor with element strides (sb, sh, st; d stride 1)
+// viewed as a 4-D map {D, T, H, B} with a {64, 128, 1, 1} box.  Rows past T
+// read as zeros.
+bool make_map(CUtensorMap* m, const void* ptr, int dtype, int D, int T, int H, int B,
+              const TensorStrides& s) {
   EncodeTiledFn enc = get_encoder();
   if (!enc) return false;
-  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)BH};
-  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)T * D * 2};
-  cuuint32_t box[3] = {64, 128, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)s.t * 2, (cuuint64_t)s.h * 2, (cuuint64_t)s.b * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(m, dtype == LKL_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                   3, const_cast<void*>(ptr), dims, strides, box, estr,
+                   4, const_cast<void*>(ptr), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
@@ -968,12 +971,21 @@ struct Maps {
   CUtensorMap qs, ks, qt, kt;
 };
 
+TensorStrides contiguous_strides(int H, int T, int D) {
+  return TensorStrides{(long long)H * T * D, (long long)T * D, (long long)D};
+}
+
+// `strides` = qs, ks, qt, kt element strides, or nullptr for contiguous tensors.
 bool build_maps(Maps& m, const Problem& p, const void* qs, const void* ks, const void* qt,
-                const void* kt) {
-  return make_map(&m.qs, qs, p.dtype_s, p.Ds, p.T, p.B * p.Hq) &&
-         make_map(&m.ks, ks, p.dtype_s, p.Ds, p.T, p.B * p.Hkv_s) &&
-         make_map(&m.qt, qt, p.dtype_t, p.Dt, p.T, p.B * p.Hq) &&
-         make_map(&m.kt, kt, p.dtype_t, p.Dt, p.T, p.B * p.Hkv_t);
+                const void* kt, const TensorStrides* strides) {
+  const TensorStrides s0 = strides ? strides[0] : contiguous_strides(p.Hq, p.T, p.Ds);
+  const TensorStrides s1 = strides ? strides[1] : contiguous_strides(p.Hkv_s, p.T, p.Ds);
+  const TensorStrides s2 = strides ? strides[2] : contiguous_strides(p.Hq, p.T, p.Dt);
+  const TensorStrides s3 = strides ? strides[3] : contiguous_strides(p.Hkv_t, p.T, p.Dt);
+  return make_map(&m.qs, qs, p.dtype_s, p.Ds, p.T, p.Hq, p.B, s0) &&
+         make_map(&m.ks, ks, p.dtype_s, p.Ds, p.T, p.Hkv_s, p.B, s1) &&
+         make_map(&m.qt, qt, p.dtype_t, p.Dt, p.T, p.Hq, p.B, s2) &&
+         make_map(&m.kt, kt, p.dtype_t, p.Dt, p.T, p.Hkv_t, p.B, s3);
 }
 
 template <int DS, int DT>
@@ -1094,11 +1106,11 @@ bool sm100_supports(const Problem& p) { return sm100_shape_ok(p) && get_encoder(
 int sm100_num_partials(const Problem& p) { return p.B * p.Hq * ((p.T + kBM - 1) / kBM); }
 
 cudaError_t launch_sm100_forward(const Problem& p, const void* qs, const void* ks,
-                                 const void* qt, const void* kt, const uint32_t* bits,
-                                 float* lse_s, float* lse_t, float* partials,
-                                 int* num_partials, cudaStream_t st) {
+                                 const void* qt, const void* kt, const TensorStrides* strides,
+                                 const uint32_t* bits, float* lse_s, float* lse_t,
+                                 float* partials, int* num_partials, cudaStream_t st) {
   Maps m;
-  if (!build_maps(m, p, qs, ks, qt, kt)) return cudaErrorInvalidValue;
+  if (!build_maps(m, p, qs, ks, qt, kt, strides)) return cudaErrorInvalidValue;
   if (num_partials) *num_partials = sm100_num_partials(p);
   if (p.Ds == 128 && p.Dt == 128) return run_forward<128, 128>(p, m, bits, lse_s, lse_t, partials, st);
   if (p.Ds == 64 && p.Dt == 64) return run_forward<64, 64>(p, m, bits, lse_s, lse_t, partials, st);
@@ -1125,15 +1137,16 @@ size_t sm100_dbuf_min_bytes(const Problem& p) {
 
 cudaError_t launch_sm100_backward(const Problem& p, const void* qs, const void* ks,
                                   const float* lse_s, const void* qt, const void* kt,
-                                  const float* lse_t, const uint32_t* bits, const float* dloss,
-                                  float* dq, float* dk, bool alias, float2* lsc, void* dbuf,
-                                  size_t dbuf_bytes, cudaStream_t st) {
+                                  const float* lse_t, const TensorStrides* strides,
+                                  const uint32_t* bits, const float* dloss, float* dq, float* dk,
+                                  bool alias, float2* lsc, void* dbuf, size_t dbuf_bytes,
+                                  cudaStream_t st) {
   std::vector<Chunk> plan;
   bool zero_dq = false;
   if (!plan_chunks(p, (long long)(dbuf_bytes / kDTileBytes), alias, plan, zero_dq))
     return cudaErrorInvalidValue;
   Maps m;
-  if (!build_maps(m, p, qs, ks, qt, kt)) return cudaErrorInvalidValue;
+  if (!build_maps(m, p, qs, ks, qt, kt, strides)) return cudaErrorInvalidValue;
   const size_t rows = (size_t)p.B * p.Hq * p.T;
   const int grid = (int)((rows + 255) / 256 < 4096 ? (rows + 255) / 256 : 4096);
   scale_lse_kernel<<<grid, 256, 0, st>>>(lse_s, lse_t, bits, p.B, p.Hq, p.T, lsc);

@@ -27,12 +27,12 @@ def test_library_loads_and_exports_header_symbols():
     assert set(names) == set(_lib.EXPORTS)
     for n in names:
         assert hasattr(L, n), n
-    assert L.lkl_abi_version() == 2
+    assert L.lkl_abi_version() == 3
 
 
 def test_status_strings():
     L = _lib.lib()
-    for code in range(12):
+    for code in range(13):
         assert L.lkl_status_string(code)
     assert L.lkl_status_string(0) == b"ok"
 
@@ -165,3 +165,28 @@ def test_wrapper_has_no_tensor_math():
         src = inspect.getsource(fn).lower()
         for key in banned:
             assert key not in src, f"{fn.__qualname__} contains {key}"
+
+
+def test_strided_entry_points_validate_before_device():
+    L = _lib.lib()
+    p = _prob(Hkv_t=2)
+    fake = ctypes.c_void_p(0x10000)
+    good = (_lib.LKLStrides * 4)(*[_lib.LKLStrides(b=300 * 4 * 128, h=128, t=4 * 128)] * 4)
+    odd = (_lib.LKLStrides * 4)(*[_lib.LKLStrides(b=300 * 4 * 128, h=128, t=4 * 128 + 4)] * 4)
+    zero = (_lib.LKLStrides * 4)(*[_lib.LKLStrides(b=0, h=128, t=512)] * 4)
+    n = 1 << 20
+    f = L.lkl_forward_strided
+    assert f(fake, fake, fake, fake, None, None, ctypes.byref(p), fake, fake, fake, fake, n,
+             None) == 1
+    assert f(fake, fake, fake, fake, odd, None, ctypes.byref(p), fake, fake, fake, fake, n,
+             None) == 5
+    assert f(fake, fake, fake, fake, zero, None, ctypes.byref(p), fake, fake, fake, fake, n,
+             None) == 2
+    assert f(ctypes.c_void_p(0x10008), fake, fake, fake, good, None, ctypes.byref(p), fake,
+             fake, fake, fake, n, None) == 5     # base pointer not 16-byte aligned
+    b = L.lkl_backward_strided
+    other = ctypes.c_void_p(0x20000)
+    # dq == dk with qs != ks -> bad alias
+    assert b(fake, other, fake, fake, fake, fake, good, None, ctypes.byref(p), None, fake, fake,
+             fake, n, None) == 10
+    assert L.lkl_status_string(12)
