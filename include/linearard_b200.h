@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define LKL_ABI_VERSION 3
+#define LKL_ABI_VERSION 4
 
 /* element types of q/k tensors */
 enum lkl_dtype { LKL_F16 = 0, LKL_BF16 = 1 };
@@ -170,6 +170,56 @@ int32_t lkl_backward_strided(const void* qs, const void* ks, const float* lse_s,
                              const lkl_strides* strides, const void* mask,
                              const lkl_problem* p, const float* dloss, float* dq, float* dk,
                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- Grouped calls (ABI version 4) ----
+ * One call for many (relation, layer) items of one sequence, as the training
+ * loop issues them (train.py:369-402: 3 relations x L layers per
+ * micro-batch).  The forward is ONE launch over every item's row tiles and the
+ * backward one dq and one dk launch per chunk of kv groups across items, so
+ * there is one tail per call instead of one per item.
+ * `shared` gives what the items have in common (B, T, Ds, Dt, dtypes, causal,
+ * mask dtype, scales; its Hq / Hkv_s / Hkv_t are ignored); the mask is shared.
+ * Every item must be on the tensor-core path (contiguous 16-byte-aligned
+ * inputs, Ds and Dt in {64, 128}; Hkv_s == Hkv_t for the backward), else
+ * LKL_ERR_UNSUPPORTED.  At most LKL_MAX_GROUP_ITEMS items (LKL_ERR_TOO_LARGE).
+ * The item table (tensor maps and pointers, 576 B per item) goes to the device
+ * inside the call through a pinned host ring that the library allocates once
+ * (8 MiB, the only host allocation it makes), so the call does not wait for
+ * the stream.
+ * Results equal the per-item calls: lkl_forward_grouped writes each item's
+ * lse_s, lse_t and losses[i] (device fp32 [n], the row-KL sum of item i);
+ * lkl_backward_grouped reads them and writes each item's dq and dk (dq == dk:
+ * fused, needs qs == ks and Hkv_s == Hq), each multiplied by dlosses[i]
+ * (device fp32 [n]; NULL = 1). */
+#define LKL_MAX_GROUP_ITEMS 1024
+
+typedef struct lkl_group_item {
+  const void* qs;      /* [B, Hq, T, Ds]     */
+  const void* ks;      /* [B, Hkv_s, T, Ds]  */
+  const void* qt;      /* [B, Hq, T, Dt]     */
+  const void* kt;      /* [B, Hkv_t, T, Dt]  */
+  int32_t Hq, Hkv_s, Hkv_t;
+  int32_t reserved;    /* 0 */
+  float* lse_s;        /* [B, Hq, T] fp32    */
+  float* lse_t;
+  float* dq;           /* [B, Hq, T, Ds] fp32 (backward) */
+  float* dk;           /* [B, Hkv_s, T, Ds] fp32 (backward) */
+} lkl_group_item;
+
+/* Scratch for a grouped forward (backward = 0) or backward (backward = 1):
+ * partials, packed mask, LSE offsets, the item table and, for the backward,
+ * the D-tile buffer (all tiles up to 8 GiB; at least one kv group). */
+size_t lkl_grouped_workspace_size(int32_t n, const lkl_group_item* items,
+                                  const lkl_problem* shared, int32_t has_mask,
+                                  int32_t backward);
+
+int32_t lkl_forward_grouped(int32_t n, const lkl_group_item* items, const void* mask,
+                            const lkl_problem* shared, float* losses, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+int32_t lkl_backward_grouped(int32_t n, const lkl_group_item* items, const void* mask,
+                             const lkl_problem* shared, const float* dlosses, void* workspace,
+                             size_t workspace_bytes, void* stream);
 
 /* Device-side error word of the current device: the bounded waits inside the
  * tensor-core kernels set it instead of hanging.  Reads (synchronously) and

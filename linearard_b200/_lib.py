@@ -12,7 +12,7 @@ import threading
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "liblinearard_b200.so")
 
-__all__ = ["LKLProblem", "LKLStrides", "lib", "check", "LKLError",
+__all__ = ["LKLProblem", "LKLStrides", "LKLGroupItem", "lib", "check", "LKLError",
            "LKL_F16", "LKL_BF16", "MASK_DTYPES", "STATUS"]
 
 LKL_F16, LKL_BF16 = 0, 1
@@ -31,7 +31,8 @@ EXPORTS = ("lkl_abi_version", "lkl_status_string", "lkl_workspace_size", "lkl_ls
            "lkl_kl_forward", "lkl_forward", "lkl_backward", "lkl_device_status",
            "lkl_last_path", "lkl_set_force_generic", "lkl_forward_noalloc",
            "lkl_last_cuda_error", "lkl_backward_workspace_size", "lkl_forward_strided",
-           "lkl_backward_strided")
+           "lkl_backward_strided", "lkl_grouped_workspace_size", "lkl_forward_grouped",
+           "lkl_backward_grouped")
 
 
 class LKLProblem(ctypes.Structure):
@@ -47,6 +48,15 @@ class LKLProblem(ctypes.Structure):
 class LKLStrides(ctypes.Structure):
     """Element strides (b, h, t) of a [B, H, T, D] input whose d stride is 1."""
     _fields_ = [("b", ctypes.c_int64), ("h", ctypes.c_int64), ("t", ctypes.c_int64)]
+
+
+class LKLGroupItem(ctypes.Structure):
+    """One (relation, layer) item of a grouped call (struct lkl_group_item)."""
+    _fields_ = [("qs", ctypes.c_void_p), ("ks", ctypes.c_void_p), ("qt", ctypes.c_void_p),
+                ("kt", ctypes.c_void_p), ("Hq", ctypes.c_int32), ("Hkv_s", ctypes.c_int32),
+                ("Hkv_t", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("lse_s", ctypes.c_void_p), ("lse_t", ctypes.c_void_p),
+                ("dq", ctypes.c_void_p), ("dk", ctypes.c_void_p)]
 
 
 class LKLError(RuntimeError):
@@ -93,6 +103,13 @@ def _declare(L):
     L.lkl_backward_strided.restype = _i32
     L.lkl_backward_strided.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _S, _vp, _P, _vp, _vp, _vp,
                                        _vp, _sz, _vp]
+    _G = ctypes.POINTER(LKLGroupItem)
+    L.lkl_grouped_workspace_size.restype = _sz
+    L.lkl_grouped_workspace_size.argtypes = [_i32, _G, _P, _i32, _i32]
+    L.lkl_forward_grouped.restype = _i32
+    L.lkl_forward_grouped.argtypes = [_i32, _G, _vp, _P, _vp, _vp, _sz, _vp]
+    L.lkl_backward_grouped.restype = _i32
+    L.lkl_backward_grouped.argtypes = [_i32, _G, _vp, _P, _vp, _vp, _sz, _vp]
     L.lkl_forward_noalloc.restype = _i32
     L.lkl_forward_noalloc.argtypes = [_vp, _vp, _vp, _vp, _vp, _P, _vp, _vp, _vp, _vp]
 

@@ -6,7 +6,9 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <atomic>
+#include <vector>
 
 #include "lkl_common.cuh"
 
@@ -350,9 +352,147 @@ int32_t backward_impl(const void* qs, const void* ks, const float* lse_s, const 
   return launch_status(e);
 }
 
+// ---------------------------------------------------------------- grouped calls
+// Problem of item i of a grouped call (shared fields + the item's heads).
+lkl_problem item_problem(const lkl_problem* shared, const lkl_group_item& it) {
+  lkl_problem q = *shared;
+  q.Hq = it.Hq;
+  q.Hkv_s = it.Hkv_s;
+  q.Hkv_t = it.Hkv_t;
+  return q;
+}
+
+// Validation of a grouped call; fills `specs`.  backward: also the gradient rules.
+int32_t check_group(int32_t n, const lkl_group_item* items, const lkl_problem* shared,
+                    bool backward, std::vector<lkl::GroupSpec>& specs) {
+  if (!items || !shared) return LKL_ERR_NULL_POINTER;
+  if (n <= 0) return LKL_ERR_BAD_SHAPE;
+  if (n > LKL_MAX_GROUP_ITEMS) return LKL_ERR_TOO_LARGE;
+  specs.clear();
+  for (int i = 0; i < n; ++i) {
+    const lkl_group_item& it = items[i];
+    const lkl_problem q = item_problem(shared, it);
+    int32_t s = check_problem(&q, true);
+    if (s) return s;
+    if (!it.qs || !it.ks || !it.qt || !it.kt || !it.lse_s || !it.lse_t) return LKL_ERR_NULL_POINTER;
+    if (!aligned(it.lse_s, 4) || !aligned(it.lse_t, 4)) return LKL_ERR_MISALIGNED;
+    const Problem pp = to_problem(&q);
+    if (!lkl::sm100_shape_ok(pp) || !aligned(it.qs, 16) || !aligned(it.ks, 16) ||
+        !aligned(it.qt, 16) || !aligned(it.kt, 16))
+      return LKL_ERR_UNSUPPORTED;
+    if (backward) {
+      if (!it.dq || !it.dk) return LKL_ERR_NULL_POINTER;
+      if (!aligned(it.dq, 16) || !aligned(it.dk, 16)) return LKL_ERR_MISALIGNED;
+      if (it.dq == it.dk && (it.qs != it.ks || it.Hkv_s != it.Hq)) return LKL_ERR_BAD_ALIAS;
+      if (it.Hkv_s != it.Hkv_t) return LKL_ERR_UNSUPPORTED;
+    }
+    lkl::GroupSpec g{};
+    g.qs = it.qs;
+    g.ks = it.ks;
+    g.qt = it.qt;
+    g.kt = it.kt;
+    g.Hq = it.Hq;
+    g.Hkv_s = it.Hkv_s;
+    g.Hkv_t = it.Hkv_t;
+    g.lse_s = it.lse_s;
+    g.lse_t = it.lse_t;
+    g.dq = it.dq;
+    g.dk = it.dk;
+    specs.push_back(g);
+  }
+  return LKL_OK;
+}
+
+// Grouped workspace: [mask bits][partials][lse offsets][item table][D tiles].
+struct GroupLayout {
+  size_t bits, partials, lsc, desc, dbuf, total;
+};
+
+GroupLayout group_layout(int32_t n, const lkl_group_item* items, const lkl_problem* shared,
+                         bool has_mask, bool backward, const std::vector<lkl::GroupSpec>& specs) {
+  long long heads = 0;
+  for (int i = 0; i < n; ++i) heads += (long long)shared->B * items[i].Hq;
+  const long long n_t = (shared->T + 127) / 128;
+  GroupLayout l{};
+  l.bits = has_mask ? bits_bytes(shared) : 0;
+  l.partials = round256((size_t)(heads * n_t) * sizeof(float));
+  l.lsc = round256((size_t)heads * shared->T * 2 * sizeof(float));
+  const Problem base = to_problem(shared);
+  l.desc = lkl::sm100_group_desc_bytes(base, specs.data(), n);
+  l.dbuf = backward ? round256(lkl::sm100_group_dbuf_bytes(base, specs.data(), n)) : 0;
+  l.total = l.bits + l.partials + l.lsc + l.desc + l.dbuf;
+  return l;
+}
+
 }  // namespace
 
 extern "C" {
+
+size_t lkl_grouped_workspace_size(int32_t n, const lkl_group_item* items,
+                                  const lkl_problem* shared, int32_t has_mask,
+                                  int32_t backward) {
+  std::vector<lkl::GroupSpec> specs;
+  if (check_group(n, items, shared, backward != 0, specs) != LKL_OK) return 0;
+  if (shared->B <= 0 || shared->T <= 0) return 0;
+  return group_layout(n, items, shared, has_mask != 0, backward != 0, specs).total;
+}
+
+int32_t lkl_forward_grouped(int32_t n, const lkl_group_item* items, const void* mask,
+                            const lkl_problem* shared, float* losses, void* ws, size_t ws_bytes,
+                            void* stream) {
+  std::vector<lkl::GroupSpec> specs;
+  int32_t s = check_group(n, items, shared, false, specs);
+  if (s) return s;
+  if (!losses) return LKL_ERR_NULL_POINTER;
+  if (!aligned(losses, 4)) return LKL_ERR_MISALIGNED;
+  if ((s = check_mask(mask, shared->mask_dtype))) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (shared->B == 0 || shared->T == 0)
+    return launch_status(cudaMemsetAsync(losses, 0, sizeof(float) * n, st));
+  const GroupLayout l = group_layout(n, items, shared, mask != nullptr, false, specs);
+  if (!ws || ws_bytes < l.total || !aligned(ws, 256)) return LKL_ERR_WORKSPACE;
+  if (!bind_device_of(items[0].qs) || !device_is_sm100()) return LKL_ERR_NO_DEVICE;
+  if (g_force_generic.load() || !lkl::sm100_supports(to_problem(shared))) return LKL_ERR_UNSUPPORTED;
+  uint32_t* bits;
+  if ((s = prepare_mask(shared, mask, ws, &bits, st))) return s;
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  float* part = reinterpret_cast<float*>(w + l.bits);
+  void* desc = w + l.bits + l.partials + l.lsc;
+  t_last_path = 1;
+  return launch_status(lkl::launch_sm100_forward_grouped(to_problem(shared), specs.data(), n,
+                                                         bits, desc, part, losses, st));
+}
+
+int32_t lkl_backward_grouped(int32_t n, const lkl_group_item* items, const void* mask,
+                             const lkl_problem* shared, const float* dlosses, void* ws,
+                             size_t ws_bytes, void* stream) {
+  std::vector<lkl::GroupSpec> specs;
+  int32_t s = check_group(n, items, shared, true, specs);
+  if (s) return s;
+  if (dlosses && !aligned(dlosses, 4)) return LKL_ERR_MISALIGNED;
+  if ((s = check_mask(mask, shared->mask_dtype))) return s;
+  if (shared->B == 0 || shared->T == 0) return LKL_OK;
+  for (int i = 0; i < n; ++i) specs[i].dloss = dlosses ? dlosses + i : nullptr;
+  const GroupLayout l = group_layout(n, items, shared, mask != nullptr, true, specs);
+  if (!ws || !aligned(ws, 256)) return LKL_ERR_WORKSPACE;
+  // a smaller D buffer runs in more chunks, down to one kv group of the largest item
+  const size_t min_dbuf = lkl::sm100_group_dbuf_min_bytes(to_problem(shared), specs.data(), n);
+  const size_t fixed = l.total - l.dbuf;
+  if (ws_bytes < fixed + min_dbuf) return LKL_ERR_WORKSPACE;
+  if (!bind_device_of(items[0].qs) || !device_is_sm100()) return LKL_ERR_NO_DEVICE;
+  if (g_force_generic.load() || !lkl::sm100_supports(to_problem(shared))) return LKL_ERR_UNSUPPORTED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t* bits;
+  if ((s = prepare_mask(shared, mask, ws, &bits, st))) return s;
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  float2* lsc = reinterpret_cast<float2*>(w + l.bits + l.partials);
+  void* desc = w + l.bits + l.partials + l.lsc;
+  void* dbuf = w + fixed;
+  t_last_path = 1;
+  return launch_status(lkl::launch_sm100_backward_grouped(to_problem(shared), specs.data(), n,
+                                                          bits, desc, lsc, dbuf,
+                                                          ws_bytes - fixed, st));
+}
 
 int32_t lkl_forward(const void* qs, const void* ks, const void* qt, const void* kt,
                     const void* mask, const lkl_problem* p, float* lse_s, float* lse_t,

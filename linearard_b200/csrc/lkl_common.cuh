@@ -65,6 +65,9 @@ cudaError_t launch_pack_mask(const void* mask, int mdt, int B, int T, uint32_t* 
                              cudaStream_t st);
 // Sums n partials in a fixed order into *out.
 cudaError_t launch_reduce_partials(const float* partials, int n, float* out, cudaStream_t st);
+// out[k] = sum of partials [begins[k], begins[k + 1]), k < n_ranges (device begins).
+cudaError_t launch_reduce_partial_ranges(const float* partials, const int* begins, int n_ranges,
+                                         float* out, cudaStream_t st);
 
 // Generic CUDA-core kernels (any supported head dim).
 // mode 0: lse of the student pair only; 1: fused lse_s, lse_t, KL partials;
@@ -83,6 +86,17 @@ int generic_num_partials(const Problem& p);
 // sm_100a tensor-core kernels.
 bool sm100_supports(const Problem& p);
 int sm100_num_partials(const Problem& p);
+// One item of a grouped call (relations / layers of one sequence): the
+// per-item tensors, head counts and outputs.  Items share B, T, the head
+// dims, dtypes, causal flag, scales and mask (the Problem passed beside them).
+struct GroupSpec {
+  const void *qs, *ks, *qt, *kt;
+  int Hq, Hkv_s, Hkv_t;
+  float *lse_s, *lse_t;  // forward outputs, backward inputs
+  float *dq, *dk;        // backward outputs; dq == dk = fused (qs == ks)
+  const float* dloss;    // backward: device scalar or nullptr (= 1)
+};
+
 // Element strides of a [B][H][T][D] input (the d stride is 1).
 struct TensorStrides {
   long long b, h, t;
@@ -102,6 +116,21 @@ bool sm100_backward_supports(const Problem& p);
 size_t sm100_dbuf_bytes(const Problem& p);
 // Smallest D buffer the backward runs with (one query-tile row of a kv group).
 size_t sm100_dbuf_min_bytes(const Problem& p);
+
+// Grouped calls (all items on the tensor-core path; `base` holds the shared
+// fields).  `desc` is sm100_group_desc_bytes(n) of device scratch for the
+// item table; the forward writes each item's LSEs and losses[i]; the backward
+// needs a D buffer of at least one kv group of the largest item
+// (sm100_group_dbuf_bytes gives the preferred size).
+size_t sm100_group_desc_bytes(const Problem& base, const GroupSpec* items, int n);
+size_t sm100_group_dbuf_bytes(const Problem& base, const GroupSpec* items, int n);
+size_t sm100_group_dbuf_min_bytes(const Problem& base, const GroupSpec* items, int n);
+cudaError_t launch_sm100_forward_grouped(const Problem& base, const GroupSpec* items, int n,
+                                         const uint32_t* bits, void* desc, float* partials,
+                                         float* losses, cudaStream_t st);
+cudaError_t launch_sm100_backward_grouped(const Problem& base, const GroupSpec* items, int n,
+                                          const uint32_t* bits, void* desc, float2* lsc,
+                                          void* dbuf, size_t dbuf_bytes, cudaStream_t st);
 cudaError_t launch_sm100_backward(const Problem& p, const void* qs, const void* ks,
                                   const float* lse_s, const void* qt, const void* kt,
                                   const float* lse_t, const TensorStrides* strides,

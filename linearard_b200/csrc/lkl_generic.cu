@@ -35,17 +35,25 @@ __global__ void pack_mask_kernel(const void* mask, int mdt, int B, int T, uint32
   }
 }
 
-__global__ void reduce_partials_kernel(const float* partials, int n, float* out) {
+// Block k sums partials [begins[k], begins[k + 1]) (all n when begins is
+// null) into out[k], in the same fixed order for every range.
+__global__ void reduce_partials_kernel(const float* partials, int n, const int* begins,
+                                       float* out) {
   __shared__ double red[32];
+  int lo = 0, hi = n;
+  if (begins) {
+    lo = begins[blockIdx.x];
+    hi = begins[blockIdx.x + 1];
+  }
   double s = 0.0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) s += (double)partials[i];
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) s += (double)partials[i];
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
   __syncthreads();
   if (threadIdx.x < 32) {
     s = (threadIdx.x < (blockDim.x >> 5)) ? red[threadIdx.x] : 0.0;
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (threadIdx.x == 0) *out = (float)s;
+    if (threadIdx.x == 0) out[blockIdx.x] = (float)s;
   }
 }
 
@@ -372,7 +380,14 @@ cudaError_t launch_pack_mask(const void* mask, int mdt, int B, int T, uint32_t* 
 }
 
 cudaError_t launch_reduce_partials(const float* partials, int n, float* out, cudaStream_t st) {
-  reduce_partials_kernel<<<1, 1024, 0, st>>>(partials, n, out);
+  reduce_partials_kernel<<<1, 1024, 0, st>>>(partials, n, nullptr, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_reduce_partial_ranges(const float* partials, const int* begins, int n_ranges,
+                                         float* out, cudaStream_t st) {
+  if (n_ranges <= 0) return cudaSuccess;
+  reduce_partials_kernel<<<n_ranges, 1024, 0, st>>>(partials, 0, begins, out);
   return cudaGetLastError();
 }
 

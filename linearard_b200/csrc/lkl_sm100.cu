@@ -28,6 +28,7 @@
 #include <math_constants.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 #include <vector>
 
@@ -125,16 +126,61 @@ struct Tile {
   int b, h, hs, ht, mt, n_ct, bh;
 };
 
-__device__ __forceinline__ Tile tile_of(const Problem& p) {
+// One item of a grouped call (several relations / layers of one sequence in
+// one launch), in device memory: everything that differs between items.  The
+// items share B, T, the head dims, dtypes, causal flag, scales and mask.
+// Global query heads (and kv groups) number the items' heads one item after
+// the other: item k owns heads [head_begin, head_begin + B*Hq).
+struct alignas(64) GroupItem {
+  CUtensorMap qs, ks, qt, kt;
+  int Hq, Hkv_s, Hkv_t;
+  int head_begin;  // first global query head
+  int grp_begin;   // first global kv group (B * Hkv_s per item)
+  int alias;       // dq == dk (qs is ks)
+  float* lse_s;
+  float* lse_t;
+  float* dq;
+  float* dk;
+  const float* dloss;
+};
+
+// Device view of a grouped call: the items and, per global query head and
+// per global kv group, the index of its item (one load per lookup).  items ==
+// nullptr: a single problem passed by value.
+struct GroupRef {
+  const GroupItem* items;
+  const int* head_item;
+  const int* group_item;
+};
+
+__device__ __forceinline__ const GroupItem* item_of_head(const GroupRef& g, int head) {
+  return g.items ? g.items + g.head_item[head] : nullptr;
+}
+
+__device__ __forceinline__ const GroupItem* item_of_group(const GroupRef& g, int grp) {
+  return g.items ? g.items + g.group_item[grp] : nullptr;
+}
+
+// Problem of one item: the shared fields of `p` with the item's head counts.
+__device__ __forceinline__ Problem item_problem(const Problem& p, const GroupItem* it) {
+  Problem q = p;
+  if (it) {
+    q.Hq = it->Hq;
+    q.Hkv_s = it->Hkv_s;
+    q.Hkv_t = it->Hkv_t;
+  }
+  return q;
+}
+
+// Tile of CTA `blk` (counted from the first CTA of its item).
+__device__ __forceinline__ Tile tile_of(const Problem& p, int blk) {
   Tile t;
   const int n_mt = (p.T + kBM - 1) / kBM;
-  const int BH = p.B * p.Hq;
   // Head-major order, longest (latest) row tiles of each head first: the CTAs
   // resident at any time work on one or two heads, so those heads' K tiles and
   // gradient rows stay in L2 instead of every head's at once.
-  (void)BH;
-  t.bh = (int)(blockIdx.x / n_mt);
-  t.mt = n_mt - 1 - (int)(blockIdx.x % n_mt);
+  t.bh = blk / n_mt;
+  t.mt = n_mt - 1 - blk % n_mt;
   t.b = t.bh / p.Hq;
   t.h = t.bh % p.Hq;
   t.hs = t.h / (p.Hq / p.Hkv_s);
@@ -192,19 +238,30 @@ __device__ __forceinline__ void setup_cta(Misc* misc, int warp, int lane) {
 // ============================================================== forward
 template <int DS, int DT>
 __global__ void __launch_bounds__(kThreads, 1)
-sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs,
-                     const __grid_constant__ CUtensorMap tm_ks,
-                     const __grid_constant__ CUtensorMap tm_qt,
-                     const __grid_constant__ CUtensorMap tm_kt, const Problem p,
-                     const uint32_t* __restrict__ bits, float* __restrict__ lse_s,
-                     float* __restrict__ lse_t, float* __restrict__ partials) {
+sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs0,
+                     const __grid_constant__ CUtensorMap tm_ks0,
+                     const __grid_constant__ CUtensorMap tm_qt0,
+                     const __grid_constant__ CUtensorMap tm_kt0, const Problem p0,
+                     const uint32_t* __restrict__ bits, float* __restrict__ lse_s0,
+                     float* __restrict__ lse_t0, float* __restrict__ partials,
+                     const GroupRef gref) {
   using L = FwdLayout<DS, DT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   Misc* misc = reinterpret_cast<Misc*>(smem + L::OFF_MISC);
   float* stat = reinterpret_cast<float*>(smem + L::OFF_STAT);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const Tile t = tile_of(p);
+  // grouped call: this CTA's item (its tensors, head counts and outputs)
+  const int n_mt = (p0.T + kBM - 1) / kBM;
+  const GroupItem* it = item_of_head(gref, (int)(blockIdx.x / n_mt));
+  const Problem p = item_problem(p0, it);
+  const CUtensorMap& tm_qs = it ? it->qs : tm_qs0;
+  const CUtensorMap& tm_ks = it ? it->ks : tm_ks0;
+  const CUtensorMap& tm_qt = it ? it->qt : tm_qt0;
+  const CUtensorMap& tm_kt = it ? it->kt : tm_kt0;
+  float* lse_s = it ? it->lse_s : lse_s0;
+  float* lse_t = it ? it->lse_t : lse_t0;
+  const Tile t = tile_of(p, (int)blockIdx.x - (it ? it->head_begin * n_mt : 0));
   int* err = &g_device_error;
   volatile int* abort = &misc->abort;
 
@@ -524,9 +581,15 @@ __device__ __forceinline__ void tile_row_to_tmem(const uint8_t* tile, int r, uin
 // One backward chunk: kv groups [bk0, bk0 + nk) (query heads bk0*G ..), query
 // tiles [i0, i1) of each; their D tiles are stored in the D buffer,
 // head-major, row tile by row tile (tiles j <= i per row when causal).
+// One backward chunk: global query heads [h0, h1) = the heads of global kv
+// groups [g0, g1), query tiles [i0, i1) of each.  Their D tiles are stored in
+// the D buffer head after head, row tile by row tile (tiles j <= i per row
+// when causal).  Without grouping, global heads and groups are the problem's
+// own (b * H + h).
 struct Chunk {
-  int bk0, nk, i0, i1;
+  int h0, h1, g0, g1, i0, i1;
   int dq_acc;            // dq adds into the output (alias, non-causal, split rows)
+  int band;              // dk: kv groups per band of work items (their Qs tiles fit L2)
   long long tph;         // D tiles per query head in this chunk
 };
 
@@ -544,12 +607,13 @@ constexpr int kDTileElems = kBM * kBN;  // one D tile: [128 query rows][128 key 
 // stores D to the D buffer for the dk launch.
 template <int DS, int DT, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
-sm100_dq_kernel(const __grid_constant__ CUtensorMap tm_qs,
-                const __grid_constant__ CUtensorMap tm_ks,
-                const __grid_constant__ CUtensorMap tm_qt,
-                const __grid_constant__ CUtensorMap tm_kt, const Problem p, const Chunk c,
+sm100_dq_kernel(const __grid_constant__ CUtensorMap tm_qs0,
+                const __grid_constant__ CUtensorMap tm_ks0,
+                const __grid_constant__ CUtensorMap tm_qt0,
+                const __grid_constant__ CUtensorMap tm_kt0, const Problem p0, const Chunk c,
                 const float2* __restrict__ lsc, const uint32_t* __restrict__ bits,
-                const float* __restrict__ dloss, float* out, uint16_t* __restrict__ dbuf) {
+                const float* __restrict__ dloss0, float* out0, uint16_t* __restrict__ dbuf,
+                const GroupRef gref) {
   using L = GradLayout<DS, DT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -564,12 +628,21 @@ sm100_dq_kernel(const __grid_constant__ CUtensorMap tm_qs,
   static_assert(kColD + kBN / 2 <= kTmemCols, "TMEM budget");
 
   // ---- work of this CTA (head-major, longest first)
+  const int n_i = c.i1 - c.i0;
+  const int local = (int)(blockIdx.x / n_i);               // head within the chunk
+  const int st_tile = c.i1 - 1 - (int)(blockIdx.x % n_i);  // descending = longest first
+  const int gh = c.h0 + local;                             // global query head
+  const GroupItem* it = item_of_head(gref, gh);
+  const Problem p = item_problem(p0, it);
+  const CUtensorMap& tm_qs = it ? it->qs : tm_qs0;
+  const CUtensorMap& tm_ks = it ? it->ks : tm_ks0;
+  const CUtensorMap& tm_qt = it ? it->qt : tm_qt0;
+  const CUtensorMap& tm_kt = it ? it->kt : tm_kt0;
+  const float* dloss = it ? it->dloss : dloss0;
+  float* out = it ? it->dq : out0;
   const int n_t = (p.T + kBM - 1) / kBM;
   const int G = p.Hq / p.Hkv_s;
-  const int n_i = c.i1 - c.i0;
-  const int local = (int)(blockIdx.x / n_i);
-  const int st_tile = c.i1 - 1 - (int)(blockIdx.x % n_i);  // descending = longest first
-  const int bh = c.bk0 * G + local;
+  const int bh = gh - (it ? it->head_begin : 0);           // b * Hq + h within the item
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int hs = h / G, ht = h / (p.Hq / p.Hkv_t);
   const int n_steps = p.causal ? st_tile + 1 : n_t;
@@ -661,7 +734,7 @@ sm100_dq_kernel(const __grid_constant__ CUtensorMap tm_qs,
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
     // this row's exponent offsets (-inf for rows that take no gradient)
     float2 Lrow = make_float2(-CUDART_INF_F, -CUDART_INF_F);
-    if (own_in) Lrow = lsc[(size_t)bh * p.T + own];
+    if (own_in) Lrow = lsc[(size_t)gh * p.T + own];
     const bool row_live = Lrow.x != -CUDART_INF_F;
     if (wg == 0) {
       // warpgroup 0 moves the stationary tiles (all 128 rows) into TMEM
@@ -783,9 +856,9 @@ __host__ __device__ __forceinline__ int dk_tiles_per_head(const Problem& p, cons
 
 template <int DS>
 __global__ void __launch_bounds__(kDkThreads, 1)
-sm100_dk_kernel(const __grid_constant__ CUtensorMap tm_qs, const Problem p, const Chunk c,
-                const uint16_t* __restrict__ dbuf, const float* __restrict__ dloss, float* out,
-                int alias) {
+sm100_dk_kernel(const __grid_constant__ CUtensorMap tm_qs0, const Problem p0, const Chunk c,
+                const uint16_t* __restrict__ dbuf, const float* __restrict__ dloss0, float* out0,
+                int alias0, const GroupRef gref) {
   using L = DkLayout<DS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -794,26 +867,55 @@ sm100_dk_kernel(const __grid_constant__ CUtensorMap tm_qs, const Problem p, cons
   int* err = &g_device_error;
   volatile int* abort = &misc->abort;
 
-  const int n_t = (p.T + kBM - 1) / kBM;
-  const int G = p.Hq / p.Hkv_s;
-  const int n_j = dk_tiles_per_head(p, c);
-  const int n_items = c.nk * n_j;
-  // Round rd of this CTA takes item rd * grid + b, or rd * grid + grid - 1 - b
-  // in odd rounds ("snake" order).  Items are key-tile major (j ascending =
-  // longest first when causal), so the snake evens out the CTAs' work.
-  auto item_at = [&](int rd) {
+  const int n_t = (p0.T + kBM - 1) / kBM;
+  const int n_groups = c.g1 - c.g0;
+  const int n_j = dk_tiles_per_head(p0, c);
+  const int n_work = n_groups * n_j;
+  // Round rd of this CTA takes work item rd * grid + b, or rd * grid + grid -
+  // 1 - b in odd rounds ("snake" order).  Work items come in bands of
+  // c.band kv groups, key-tile major inside a band (j ascending = longest first
+  // when causal, which the snake evens out across CTAs); the CTAs at work at
+  // any time read the Qs tiles of one or two bands, which stay in L2.
+  auto work_at = [&](int rd) {
     const int g = (int)gridDim.x, b = (int)blockIdx.x;
     return rd * g + ((rd & 1) ? g - 1 - b : b);
   };
-  // item -> (kv head of the chunk, key tile, first query tile, query tiles)
-  auto item_of = [&](int item, int& lk, int& j, int& i_first, int& n_i) {
-    j = item / c.nk;
-    lk = item % c.nk;
-    i_first = p.causal ? max(c.i0, j) : c.i0;
-    n_i = c.i1 - i_first;
+  // work item -> (kv group, key tile j, first query tile, query tiles) and the
+  // group's item (its head counts, tensors and outputs)
+  struct Work {
+    const GroupItem* it;
+    Problem p;
+    int G, b, hs, j, i_first, n_i;
+    long long head0;  // global query head of the group's first head
+  };
+  const int band = min(max(c.band, 1), n_groups);
+  const int full_bands = n_groups / band, rest = n_groups - full_bands * band;
+  auto work_of = [&](int w) {
+    Work k;
+    int lg0 = 0, r = w, size = band;
+    if (w < full_bands * band * n_j) {
+      lg0 = (w / (band * n_j)) * band;
+      r = w % (band * n_j);
+    } else {
+      lg0 = full_bands * band;
+      r = w - full_bands * band * n_j;
+      size = rest;
+    }
+    k.j = r / size;
+    const int g = c.g0 + lg0 + r % size;  // global kv group
+    k.it = item_of_group(gref, g);
+    k.p = item_problem(p0, k.it);
+    k.G = k.p.Hq / k.p.Hkv_s;
+    const int lg = g - (k.it ? k.it->grp_begin : 0);  // b * Hkv_s + hs within the item
+    k.b = lg / k.p.Hkv_s;
+    k.hs = lg % k.p.Hkv_s;
+    k.head0 = (long long)(k.it ? k.it->head_begin : 0) + (long long)k.b * k.p.Hq + k.hs * k.G;
+    k.i_first = k.p.causal ? max(c.i0, k.j) : c.i0;
+    k.n_i = c.i1 - k.i_first;
+    return k;
   };
 
-  if (warp == 0 && lane == 0) tma_prefetch_desc(&tm_qs);
+  if (warp == 0 && lane == 0 && !gref.items) tma_prefetch_desc(&tm_qs0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < 4; ++s) {
       mbar_init(&misc->k_full[s], 1);
@@ -837,27 +939,25 @@ sm100_dk_kernel(const __grid_constant__ CUtensorMap tm_qs, const Problem p, cons
 
   if (warp == 0) {
     if (lane == 0) {
-      int gs = 0;  // running stage counter over all items of this CTA
+      int gs = 0;  // running stage counter over all work items of this CTA
       bool ok = true;
-      for (int rd = 0, item = item_at(0); ok && item < n_items; item = item_at(++rd)) {
-        int lk, j, i_first, n_i;
-        item_of(item, lk, j, i_first, n_i);
-        const int bk = c.bk0 + lk;
-        for (int s = 0; s < G * n_i; ++s, ++gs) {
+      for (int rd = 0, w = work_at(0); ok && w < n_work; w = work_at(++rd)) {
+        const Work k = work_of(w);
+        const CUtensorMap* tm_qs = k.it ? &k.it->qs : &tm_qs0;
+        for (int s = 0; s < k.G * k.n_i; ++s, ++gs) {
           const int slot = gs % L::NS;
           if (gs >= L::NS &&
               !mbar_wait(&misc->k_empty[slot], ((gs / L::NS) - 1) & 1, abort, err)) {
             ok = false;
             break;
           }
-          const int g = s / n_i, i = i_first + s % n_i;
-          const long long tile =
-              (long long)(lk * G + g) * c.tph + d_row_offset(p, c, i, n_t) + j;
+          const int g = s / k.n_i, i = k.i_first + s % k.n_i;
+          const long long tile = (k.head0 + g - c.h0) * c.tph + d_row_offset(k.p, c, i, n_t) + k.j;
           uint8_t* stg = smem + slot * L::STAGE;
           mbar_arrive_expect_tx(&misc->k_full[slot], L::STAGE);
           bulk_load(stg, dbuf + tile * kDTileElems, L::DT_BYTES, &misc->k_full[slot]);
-          issue_tile_loads(stg + L::DT_BYTES, &tm_qs, &misc->k_full[slot], DS, i * kBM,
-                           (bk % p.Hkv_s) * G + g, bk / p.Hkv_s);
+          issue_tile_loads(stg + L::DT_BYTES, tm_qs, &misc->k_full[slot], DS, i * kBM,
+                           k.hs * k.G + g, k.b);
         }
       }
     }
@@ -865,17 +965,16 @@ sm100_dk_kernel(const __grid_constant__ CUtensorMap tm_qs, const Problem p, cons
     if (lane == 0) {
       // acc[key j][feature] += sum over query rows of D[query][key] Qs[query][feature]:
       // A = D^T (no swizzle, MN-major) and B = Qs (128B swizzle, MN-major)
-      const uint32_t id = idesc_f16(kBN, DS, p.dtype_s, p.dtype_s, 1, 1);
+      const uint32_t id = idesc_f16(kBN, DS, p0.dtype_s, p0.dtype_s, 1, 1);
       int gs = 0, it = 0;
       bool ok = true;
-      for (int rd = 0, item = item_at(0); ok && item < n_items; item = item_at(++rd), ++it) {
-        int lk, j, i_first, n_i;
-        item_of(item, lk, j, i_first, n_i);
+      for (int rd = 0, w = work_at(0); ok && w < n_work; w = work_at(++rd), ++it) {
+        const Work k = work_of(w);
         const int ab = it & 1;
         if (it >= 2 && !mbar_wait(&misc->s_empty[ab], ((it >> 1) - 1) & 1, abort, err)) break;
         tc_fence_after();
         const uint32_t acc = tmem + ab * 128;
-        for (int s = 0; s < G * n_i; ++s, ++gs) {
+        for (int s = 0; s < k.G * k.n_i; ++s, ++gs) {
           const int slot = gs % L::NS;
           if (!mbar_wait(&misc->k_full[slot], (gs / L::NS) & 1, abort, err)) {
             ok = false;
@@ -895,19 +994,21 @@ sm100_dk_kernel(const __grid_constant__ CUtensorMap tm_qs, const Problem p, cons
   } else {
     const int q = warp & 3;
     const int r = q * 32 + lane;
-    const float gscale = p.sc_s * (dloss ? *dloss : 1.f);
     int it = 0;
-    for (int rd = 0, item = item_at(0); item < n_items; item = item_at(++rd), ++it) {
-      int lk, j, i_first, n_i;
-      item_of(item, lk, j, i_first, n_i);
+    for (int rd = 0, w = work_at(0); w < n_work; w = work_at(++rd), ++it) {
+      const Work k = work_of(w);
       const int ab = it & 1;
       if (!mbar_wait(&misc->s_full[ab], (it >> 1) & 1, abort, err)) break;
       tc_fence_after();
-      const int own = j * kBN + r;  // key row of this lane
+      const int own = k.j * kBN + r;  // key row of this lane
+      const int alias = k.it ? k.it->alias : alias0;
+      const float* dloss = k.it ? k.it->dloss : dloss0;
+      float* out = k.it ? (alias ? k.it->dq : k.it->dk) : out0;
+      const float gscale = k.p.sc_s * (dloss ? *dloss : 1.f);
       // the first chunk that reaches key tile j stores, later ones add
-      const bool accumulate = alias != 0 || (p.causal ? j < c.i0 : c.i0 > 0);
-      float* row = out + ((size_t)(c.bk0 + lk) * p.T + own) * DS;
-      store_rows<DS>(tmem + ab * 128 + ((uint32_t)(q * 32) << 16), row, gscale, own < p.T,
+      const bool accumulate = alias != 0 || (k.p.causal ? k.j < c.i0 : c.i0 > 0);
+      float* row = out + (((size_t)k.b * k.p.Hkv_s + k.hs) * k.p.T + own) * DS;
+      store_rows<DS>(tmem + ab * 128 + ((uint32_t)(q * 32) << 16), row, gscale, own < k.p.T,
                      accumulate);
       tc_fence_before();
       __syncwarp();
@@ -990,20 +1091,22 @@ bool build_maps(Maps& m, const Problem& p, const void* qs, const void* ks, const
 
 template <int DS, int DT>
 cudaError_t run_forward(const Problem& p, const Maps& m, const uint32_t* bits, float* lse_s,
-                        float* lse_t, float* partials, cudaStream_t st) {
+                        float* lse_t, float* partials, int grid, const GroupRef& gref,
+                        cudaStream_t st) {
   using L = FwdLayout<DS, DT>;
   auto k = sm100_forward_kernel<DS, DT>;
   cudaError_t e = prep(k, L::BYTES);
   if (e != cudaSuccess) return e;
-  const int grid = sm100_num_partials(p);
-  k<<<grid, kThreads, L::BYTES, st>>>(m.qs, m.ks, m.qt, m.kt, p, bits, lse_s, lse_t, partials);
+  k<<<grid, kThreads, L::BYTES, st>>>(m.qs, m.ks, m.qt, m.kt, p, bits, lse_s, lse_t, partials,
+                                      gref);
   return cudaGetLastError();
 }
 
 template <int DS, int DT>
 cudaError_t run_grad(const Problem& p, const Maps& m, const std::vector<Chunk>& plan,
                      const float2* lsc, const uint32_t* bits, const float* dloss, float* dq,
-                     float* dk, bool alias, uint16_t* dbuf, cudaStream_t st) {
+                     float* dk, bool alias, uint16_t* dbuf, const GroupRef& gref,
+                     cudaStream_t st) {
   using L = GradLayout<DS, DT>;
   using LK = DkLayout<DS>;
   const bool bf = p.dtype_s == LKL_BF16;
@@ -1016,18 +1119,17 @@ cudaError_t run_grad(const Problem& p, const Maps& m, const std::vector<Chunk>& 
   if ((e = cudaGetDevice(&dev)) != cudaSuccess ||
       (e = cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
     return e;
-  const int G = p.Hq / p.Hkv_s;
   for (const Chunk& c : plan) {
     // dq rows of the chunk (stores D); then dk, which in the fused case adds
     // into rows that dq has already written.  (Running the HBM-bound dk
     // launch beside the next chunk's dq launch was measured: no gain, the
     // chip is at its power limit either way.)
-    kq<<<c.nk * G * (c.i1 - c.i0), kThreads, L::BYTES, st>>>(m.qs, m.ks, m.qt, m.kt, p, c, lsc,
-                                                             bits, dloss, dq, dbuf);
+    kq<<<(c.h1 - c.h0) * (c.i1 - c.i0), kThreads, L::BYTES, st>>>(
+        m.qs, m.ks, m.qt, m.kt, p, c, lsc, bits, dloss, dq, dbuf, gref);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    const int grid = std::min(c.nk * dk_tiles_per_head(p, c), num_sms);
+    const int grid = std::min((c.g1 - c.g0) * dk_tiles_per_head(p, c), num_sms);
     kk<<<grid, kDkThreads, LK::BYTES, st>>>(m.qs, p, c, dbuf, dloss, alias ? dq : dk,
-                                            alias ? 1 : 0);
+                                            alias ? 1 : 0, gref);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -1035,14 +1137,22 @@ cudaError_t run_grad(const Problem& p, const Maps& m, const std::vector<Chunk>& 
 
 constexpr long long kDTileBytes = (long long)kDTileElems * 2;
 
+// kv groups per band of dk work items: the bands' Qs tiles (G heads of T rows
+// each) stay within a quarter of the 126 MB L2.
+int dk_band(const Problem& p, int G) {
+  const long long per_group = (long long)G * p.T * p.Ds * 2;
+  return (int)std::max<long long>(1, (32ll << 20) / std::max<long long>(per_group, 1));
+}
+
 long long d_tiles_per_head(const Problem& p) {
   const long long n_t = (p.T + kBM - 1) / kBM;
   return p.causal ? n_t * (n_t + 1) / 2 : n_t * n_t;
 }
 
-// Splits the backward into chunks whose D tiles fit `cap_tiles`: whole kv
-// groups when one group fits, otherwise one group at a time in ranges of
-// query tiles.  Returns false when not even one query-tile row of a group fits.
+// Splits the backward of one problem into chunks whose D tiles fit
+// `cap_tiles`: whole kv groups when one group fits, otherwise one group at a
+// time in ranges of query tiles.  Returns false when not even one query-tile
+// row of a group fits.
 bool plan_chunks(const Problem& p, long long cap_tiles, bool alias, std::vector<Chunk>& out,
                  bool& zero_dq) {
   const int n_t = (p.T + kBM - 1) / kBM;
@@ -1051,20 +1161,27 @@ bool plan_chunks(const Problem& p, long long cap_tiles, bool alias, std::vector<
   const long long group_tiles = (long long)G * d_tiles_per_head(p);
   out.clear();
   zero_dq = false;
+  auto add = [&](int g0, int g1, int i0, int i1, long long tph, int acc) {
+    Chunk c{};
+    c.g0 = g0;
+    c.g1 = g1;
+    c.h0 = g0 * G;
+    c.h1 = g1 * G;
+    c.i0 = i0;
+    c.i1 = i1;
+    c.tph = tph;
+    c.dq_acc = acc;
+    c.band = dk_band(p, G);
+    out.push_back(c);
+  };
   if (group_tiles <= cap_tiles) {
     // as few chunks as fit, of near-equal size (a small last chunk would
     // leave most SMs idle)
     const int per = (int)std::min<long long>(groups, cap_tiles / group_tiles);
     const int n_chunks = (groups + per - 1) / per;
-    for (int k = 0; k < n_chunks; ++k) {
-      Chunk c{};
-      c.bk0 = (int)((long long)k * groups / n_chunks);
-      c.nk = (int)((long long)(k + 1) * groups / n_chunks) - c.bk0;
-      c.i0 = 0;
-      c.i1 = n_t;
-      c.tph = d_tiles_per_head(p);
-      out.push_back(c);
-    }
+    for (int k = 0; k < n_chunks; ++k)
+      add((int)((long long)k * groups / n_chunks), (int)((long long)(k + 1) * groups / n_chunks),
+          0, n_t, d_tiles_per_head(p), 0);
     return true;
   }
   const bool acc = alias && !p.causal;
@@ -1078,19 +1195,167 @@ bool plan_chunks(const Problem& p, long long cap_tiles, bool alias, std::vector<
         tiles += row_tiles;
       }
       if (i1 == i0) return false;
-      Chunk c{};
-      c.bk0 = g0;
-      c.nk = 1;
-      c.i0 = i0;
-      c.i1 = i1;
-      c.tph = tiles;
-      c.dq_acc = acc ? 1 : 0;
-      out.push_back(c);
+      add(g0, g0 + 1, i0, i1, tiles, acc ? 1 : 0);
       i0 = i1;
     }
   }
   zero_dq = acc;
   return true;
+}
+
+// ---------------------------------------------------------------- grouped calls
+// Device image of a grouped call, written into the workspace: the items, the
+// partial-sum range of each item (n + 1 ints), then the item index of every
+// global query head and of every global kv group.
+size_t group_desc_bytes(int n, long long heads, long long groups) {
+  const size_t bytes = (size_t)n * sizeof(GroupItem) + (size_t)(n + 1 + heads + groups) * 4;
+  return (bytes + 255) & ~size_t(255);
+}
+
+// Pinned staging for the item tables.  A copy from pageable memory would
+// make cudaMemcpyAsync wait for the stream, so that the host could not queue
+// the launches behind it; from pinned memory it is asynchronous.  A ring of
+// slots per process; a slot is reused once the event recorded after its copy
+// has completed (it waits only when kSlots calls are still in flight).
+class PinnedRing {
+ public:
+  static constexpr int kSlots = 8;
+  static constexpr size_t kSlotBytes = 1u << 20;
+
+  // Queues a copy of `image` to `dst` on `st`.
+  cudaError_t copy(void* dst, const std::vector<uint8_t>& image, cudaStream_t st) {
+    if (image.size() > kSlotBytes) return cudaErrorInvalidValue;
+    std::lock_guard<std::mutex> lock(mu_);
+    if (!host_) {
+      cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&host_), kSlots * kSlotBytes,
+                                    cudaHostAllocPortable);
+      if (e != cudaSuccess) {
+        host_ = nullptr;
+        return e;
+      }
+    }
+    Slot& slot = slots_[next_];
+    next_ = (next_ + 1) % kSlots;
+    cudaError_t e;
+    if (slot.event && (e = cudaEventSynchronize(slot.event)) != cudaSuccess) return e;
+    uint8_t* h = host_ + (&slot - slots_) * kSlotBytes;
+    std::memcpy(h, image.data(), image.size());
+    if ((e = cudaMemcpyAsync(dst, h, image.size(), cudaMemcpyHostToDevice, st)) != cudaSuccess)
+      return e;
+    // events are tied to the device current when they are created
+    int dev = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if (slot.event && slot.device != dev) {
+      cudaEventDestroy(slot.event);
+      slot.event = nullptr;
+    }
+    if (!slot.event &&
+        (e = cudaEventCreateWithFlags(&slot.event, cudaEventDisableTiming)) != cudaSuccess)
+      return e;
+    slot.device = dev;
+    return cudaEventRecord(slot.event, st);
+  }
+
+ private:
+  struct Slot {
+    cudaEvent_t event = nullptr;
+    int device = -1;
+  };
+  std::mutex mu_;
+  uint8_t* host_ = nullptr;
+  Slot slots_[kSlots];
+  int next_ = 0;
+};
+
+PinnedRing& pinned_ring() {
+  static PinnedRing ring;
+  return ring;
+}
+
+// Host image of a grouped call for device address `desc`; *ref_dev gets the
+// device view.  group_heads (optional): query heads of every global kv group.
+bool build_group(const Problem& base, const GroupSpec* g, int n, std::vector<uint8_t>& image,
+                 GroupRef* ref_dev, const void* desc, int* total_heads,
+                 std::vector<int>* group_heads) {
+  const int n_t = (base.T + kBM - 1) / kBM;
+  long long heads = 0, groups = 0;
+  for (int i = 0; i < n; ++i) {
+    heads += (long long)base.B * g[i].Hq;
+    groups += (long long)base.B * g[i].Hkv_s;
+  }
+  if (heads * n_t > INT32_MAX) return false;
+  image.assign(group_desc_bytes(n, heads, groups), 0);
+  GroupItem* items = reinterpret_cast<GroupItem*>(image.data());
+  int* begins = reinterpret_cast<int*>(image.data() + (size_t)n * sizeof(GroupItem));
+  int* head_item = begins + n + 1;
+  int* group_item = head_item + heads;
+  int head = 0, grp = 0;
+  for (int i = 0; i < n; ++i) {
+    Problem p = base;
+    p.Hq = g[i].Hq;
+    p.Hkv_s = g[i].Hkv_s;
+    p.Hkv_t = g[i].Hkv_t;
+    Maps m;
+    if (!build_maps(m, p, g[i].qs, g[i].ks, g[i].qt, g[i].kt, nullptr)) return false;
+    GroupItem& it = items[i];
+    it.qs = m.qs;
+    it.ks = m.ks;
+    it.qt = m.qt;
+    it.kt = m.kt;
+    it.Hq = p.Hq;
+    it.Hkv_s = p.Hkv_s;
+    it.Hkv_t = p.Hkv_t;
+    it.head_begin = head;
+    it.grp_begin = grp;
+    it.alias = g[i].dq != nullptr && g[i].dq == g[i].dk;
+    it.lse_s = g[i].lse_s;
+    it.lse_t = g[i].lse_t;
+    it.dq = g[i].dq;
+    it.dk = g[i].dk;
+    it.dloss = g[i].dloss;
+    begins[i] = head * n_t;
+    for (int k = 0; k < base.B * p.Hq; ++k) head_item[head + k] = i;
+    for (int k = 0; k < base.B * p.Hkv_s; ++k) {
+      group_item[grp + k] = i;
+      if (group_heads) group_heads->push_back(p.Hq / p.Hkv_s);
+    }
+    head += base.B * p.Hq;
+    grp += base.B * p.Hkv_s;
+  }
+  begins[n] = head * n_t;
+  *total_heads = head;
+  const uint8_t* d = static_cast<const uint8_t*>(desc);
+  ref_dev->items = reinterpret_cast<const GroupItem*>(d);
+  ref_dev->head_item = reinterpret_cast<const int*>(
+      d + (reinterpret_cast<uint8_t*>(head_item) - image.data()));
+  ref_dev->group_item = reinterpret_cast<const int*>(
+      d + (reinterpret_cast<uint8_t*>(group_item) - image.data()));
+  return true;
+}
+
+cudaError_t dispatch_forward(const Problem& p, const Maps& m, const uint32_t* bits, float* lse_s,
+                             float* lse_t, float* partials, int grid, const GroupRef& g,
+                             cudaStream_t st) {
+  if (p.Ds == 128 && p.Dt == 128)
+    return run_forward<128, 128>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
+  if (p.Ds == 64 && p.Dt == 64)
+    return run_forward<64, 64>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
+  if (p.Ds == 128 && p.Dt == 64)
+    return run_forward<128, 64>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
+  return run_forward<64, 128>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
+}
+
+cudaError_t dispatch_grad(const Problem& p, const Maps& m, const std::vector<Chunk>& plan,
+                          const float2* lsc, const uint32_t* bits, const float* dloss, float* dq,
+                          float* dk, bool alias, uint16_t* dbuf, const GroupRef& g,
+                          cudaStream_t st) {
+  if (p.Ds == 128 && p.Dt == 128)
+    return run_grad<128, 128>(p, m, plan, lsc, bits, dloss, dq, dk, alias, dbuf, g, st);
+  if (p.Ds == 64 && p.Dt == 64)
+    return run_grad<64, 64>(p, m, plan, lsc, bits, dloss, dq, dk, alias, dbuf, g, st);
+  if (p.Ds == 128 && p.Dt == 64)
+    return run_grad<128, 64>(p, m, plan, lsc, bits, dloss, dq, dk, alias, dbuf, g, st);
+  return run_grad<64, 128>(p, m, plan, lsc, bits, dloss, dq, dk, alias, dbuf, g, st);
 }
 
 }  // namespace
@@ -1111,11 +1376,9 @@ cudaError_t launch_sm100_forward(const Problem& p, const void* qs, const void* k
                                  float* partials, int* num_partials, cudaStream_t st) {
   Maps m;
   if (!build_maps(m, p, qs, ks, qt, kt, strides)) return cudaErrorInvalidValue;
-  if (num_partials) *num_partials = sm100_num_partials(p);
-  if (p.Ds == 128 && p.Dt == 128) return run_forward<128, 128>(p, m, bits, lse_s, lse_t, partials, st);
-  if (p.Ds == 64 && p.Dt == 64) return run_forward<64, 64>(p, m, bits, lse_s, lse_t, partials, st);
-  if (p.Ds == 128 && p.Dt == 64) return run_forward<128, 64>(p, m, bits, lse_s, lse_t, partials, st);
-  return run_forward<64, 128>(p, m, bits, lse_s, lse_t, partials, st);
+  const int grid = sm100_num_partials(p);
+  if (num_partials) *num_partials = grid;
+  return dispatch_forward(p, m, bits, lse_s, lse_t, partials, grid, GroupRef{}, st);
 }
 
 bool sm100_backward_supports(const Problem& p) {
@@ -1154,14 +1417,102 @@ cudaError_t launch_sm100_backward(const Problem& p, const void* qs, const void* 
   if (e != cudaSuccess) return e;
   if (zero_dq && (e = cudaMemsetAsync(dq, 0, rows * p.Ds * sizeof(float), st)) != cudaSuccess)
     return e;
-  uint16_t* d16 = static_cast<uint16_t*>(dbuf);
-  if (p.Ds == 128 && p.Dt == 128)
-    return run_grad<128, 128>(p, m, plan, lsc, bits, dloss, dq, dk, alias, d16, st);
-  if (p.Ds == 64 && p.Dt == 64)
-    return run_grad<64, 64>(p, m, plan, lsc, bits, dloss, dq, dk, alias, d16, st);
-  if (p.Ds == 128 && p.Dt == 64)
-    return run_grad<128, 64>(p, m, plan, lsc, bits, dloss, dq, dk, alias, d16, st);
-  return run_grad<64, 128>(p, m, plan, lsc, bits, dloss, dq, dk, alias, d16, st);
+  return dispatch_grad(p, m, plan, lsc, bits, dloss, dq, dk, alias,
+                       static_cast<uint16_t*>(dbuf), GroupRef{}, st);
+}
+
+size_t sm100_group_desc_bytes(const Problem& base, const GroupSpec* g, int n) {
+  long long heads = 0, groups = 0;
+  for (int i = 0; i < n; ++i) {
+    heads += (long long)base.B * g[i].Hq;
+    groups += (long long)base.B * g[i].Hkv_s;
+  }
+  return group_desc_bytes(n, heads, groups);
+}
+
+size_t sm100_group_dbuf_bytes(const Problem& base, const GroupSpec* g, int n) {
+  long long all = 0, largest = 0;
+  for (int i = 0; i < n; ++i) {
+    const long long group = (long long)(g[i].Hq / g[i].Hkv_s) * d_tiles_per_head(base);
+    all += (long long)base.B * g[i].Hkv_s * group;
+    largest = std::max(largest, group);
+  }
+  return (size_t)(std::max(std::min(all, kDBufCapBytes / kDTileBytes), largest) * kDTileBytes);
+}
+
+size_t sm100_group_dbuf_min_bytes(const Problem& base, const GroupSpec* g, int n) {
+  long long largest = 0;
+  for (int i = 0; i < n; ++i)
+    largest = std::max(largest, (long long)(g[i].Hq / g[i].Hkv_s) * d_tiles_per_head(base));
+  return (size_t)(largest * kDTileBytes);
+}
+
+cudaError_t launch_sm100_forward_grouped(const Problem& base, const GroupSpec* g, int n,
+                                         const uint32_t* bits, void* desc, float* partials,
+                                         float* losses, cudaStream_t st) {
+  std::vector<uint8_t> image;
+  GroupRef ref{};
+  int heads = 0;
+  if (n <= 0 || !build_group(base, g, n, image, &ref, desc, &heads, nullptr))
+    return cudaErrorInvalidValue;
+  cudaError_t e = pinned_ring().copy(desc, image, st);
+  if (e != cudaSuccess) return e;
+  const int* begins = reinterpret_cast<const int*>(static_cast<const uint8_t*>(desc) +
+                                                   (size_t)n * sizeof(GroupItem));
+  // the kernel reads every item's maps from `items`; the by-value maps of
+  // the first item only fill the parameters
+  const GroupItem& first = *reinterpret_cast<const GroupItem*>(image.data());
+  Maps m{first.qs, first.ks, first.qt, first.kt};
+  const int grid = heads * ((base.T + kBM - 1) / kBM);
+  e = dispatch_forward(base, m, bits, nullptr, nullptr, partials, grid, ref, st);
+  if (e != cudaSuccess) return e;
+  return launch_reduce_partial_ranges(partials, begins, n, losses, st);
+}
+
+cudaError_t launch_sm100_backward_grouped(const Problem& base, const GroupSpec* g, int n,
+                                          const uint32_t* bits, void* desc, float2* lsc,
+                                          void* dbuf, size_t dbuf_bytes, cudaStream_t st) {
+  std::vector<uint8_t> image;
+  std::vector<int> group_heads;
+  GroupRef ref{};
+  int heads = 0;
+  if (n <= 0 || !build_group(base, g, n, image, &ref, desc, &heads, &group_heads))
+    return cudaErrorInvalidValue;
+  // chunks of whole kv groups (in item order) whose D tiles fit the buffer
+  const int n_t = (base.T + kBM - 1) / kBM;
+  const long long tph = d_tiles_per_head(base), cap = (long long)(dbuf_bytes / kDTileBytes);
+  std::vector<Chunk> plan;
+  for (int g0 = 0, h0 = 0; g0 < (int)group_heads.size();) {
+    int g1 = g0, h1 = h0;
+    while (g1 < (int)group_heads.size() && (long long)(h1 - h0 + group_heads[g1]) * tph <= cap)
+      h1 += group_heads[g1++];
+    if (g1 == g0) return cudaErrorInvalidValue;  // one kv group does not fit
+    Chunk c{};
+    c.g0 = g0;
+    c.g1 = g1;
+    c.h0 = h0;
+    c.h1 = h1;
+    c.i0 = 0;
+    c.i1 = n_t;
+    c.tph = tph;
+    c.band = dk_band(base, *std::max_element(group_heads.begin() + g0, group_heads.begin() + g1));
+    plan.push_back(c);
+    g0 = g1;
+    h0 = h1;
+  }
+  cudaError_t e = pinned_ring().copy(desc, image, st);
+  if (e != cudaSuccess) return e;
+  const GroupItem* host_items = reinterpret_cast<const GroupItem*>(image.data());
+  for (int i = 0; i < n; ++i) {
+    const size_t rows = (size_t)base.B * g[i].Hq * base.T;
+    const int grid = (int)((rows + 255) / 256 < 4096 ? (rows + 255) / 256 : 4096);
+    scale_lse_kernel<<<grid, 256, 0, st>>>(g[i].lse_s, g[i].lse_t, bits, base.B, g[i].Hq, base.T,
+                                           lsc + (size_t)host_items[i].head_begin * base.T);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  Maps m{host_items[0].qs, host_items[0].ks, host_items[0].qt, host_items[0].kt};
+  return dispatch_grad(base, m, plan, lsc, bits, nullptr, nullptr, nullptr, false,
+                       static_cast<uint16_t*>(dbuf), ref, st);
 }
 
 }  // namespace lkl

@@ -27,7 +27,7 @@ def test_library_loads_and_exports_header_symbols():
     assert set(names) == set(_lib.EXPORTS)
     for n in names:
         assert hasattr(L, n), n
-    assert L.lkl_abi_version() == 3
+    assert L.lkl_abi_version() == 4
 
 
 def test_status_strings():
@@ -190,3 +190,37 @@ def test_strided_entry_points_validate_before_device():
     assert b(fake, other, fake, fake, fake, fake, good, None, ctypes.byref(p), None, fake, fake,
              fake, n, None) == 10
     assert L.lkl_status_string(12)
+
+
+def test_grouped_entry_points_validate_before_device():
+    L = _lib.lib()
+    shared = _prob(Hkv_t=2)
+    fake = 0x10000
+
+    def item(Hq=4, Hkv_s=2, Hkv_t=2, dq=fake, dk=fake + 0x1000, qs=fake, ks=fake + 0x2000):
+        return _lib.LKLGroupItem(qs, ks, fake, fake, Hq, Hkv_s, Hkv_t, 0, fake, fake, dq, dk)
+
+    one = (_lib.LKLGroupItem * 1)(item())
+    n_f = L.lkl_grouped_workspace_size(1, one, ctypes.byref(shared), 0, 0)
+    n_b = L.lkl_grouped_workspace_size(1, one, ctypes.byref(shared), 0, 1)
+    assert n_f > 0 and n_f % 256 == 0
+    n_t = (300 + 127) // 128
+    assert n_b - n_f >= 4 * n_t * (n_t + 1) // 2 * 32768   # every D tile fits (< 8 GiB)
+    # head dim 32 is outside the tensor-core path
+    small = _prob(Ds=32, Dt=32, Hkv_t=2)
+    assert L.lkl_grouped_workspace_size(1, one, ctypes.byref(small), 0, 0) == 0
+    c = ctypes.c_void_p
+    assert L.lkl_forward_grouped(1, one, None, ctypes.byref(small), c(fake), c(fake), 1 << 20,
+                                 None) == 12
+    # dq == dk with qs != ks
+    bad = (_lib.LKLGroupItem * 1)(item(dq=fake, dk=fake))
+    assert L.lkl_backward_grouped(1, bad, None, ctypes.byref(shared), None, c(fake), 1 << 20,
+                                  None) == 10
+    # Hkv_s != Hkv_t: no tensor-core backward
+    mixed = (_lib.LKLGroupItem * 1)(item(Hkv_t=4))
+    assert L.lkl_backward_grouped(1, mixed, None, ctypes.byref(shared), None, c(fake), 1 << 20,
+                                  None) == 12
+    assert L.lkl_forward_grouped(0, one, None, ctypes.byref(shared), c(fake), c(fake), 1 << 20,
+                                 None) == 2
+    assert L.lkl_forward_grouped(1, one, None, ctypes.byref(shared), c(fake), c(fake), 16,
+                                 None) == 6
