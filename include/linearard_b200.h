@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define LKL_ABI_VERSION 4
+#define LKL_ABI_VERSION 5
 
 /* element types of q/k tensors */
 enum lkl_dtype { LKL_F16 = 0, LKL_BF16 = 1 };
@@ -179,8 +179,9 @@ int32_t lkl_backward_strided(const void* qs, const void* ks, const float* lse_s,
  * there is one tail per call instead of one per item.
  * `shared` gives what the items have in common (B, T, Ds, Dt, dtypes, causal,
  * mask dtype, scales; its Hq / Hkv_s / Hkv_t are ignored); the mask is shared.
- * Every item must be on the tensor-core path (contiguous 16-byte-aligned
- * inputs, Ds and Dt in {64, 128}; Hkv_s == Hkv_t for the backward), else
+ * Every item must be on the tensor-core path (16-byte-aligned inputs,
+ * contiguous or strided, Ds and Dt in {64, 128}; Hkv_s == Hkv_t for the
+ * backward), else
  * LKL_ERR_UNSUPPORTED.  At most LKL_MAX_GROUP_ITEMS items (LKL_ERR_TOO_LARGE).
  * The item table (tensor maps and pointers, 576 B per item) goes to the device
  * inside the call through a pinned host ring that the library allocates once
@@ -199,11 +200,13 @@ typedef struct lkl_group_item {
   const void* qt;      /* [B, Hq, T, Dt]     */
   const void* kt;      /* [B, Hkv_t, T, Dt]  */
   int32_t Hq, Hkv_s, Hkv_t;
-  int32_t reserved;    /* 0 */
+  int32_t strided;     /* 0: contiguous inputs; 1: use `strides` (ABI version 5) */
   float* lse_s;        /* [B, Hq, T] fp32    */
   float* lse_t;
   float* dq;           /* [B, Hq, T, Ds] fp32 (backward) */
   float* dk;           /* [B, Hkv_s, T, Ds] fp32 (backward) */
+  lkl_strides strides[4];  /* qs, ks, qt, kt element strides when `strided`, as
+                              for lkl_forward_strided (multiples of 8 elements) */
 } lkl_group_item;
 
 /* Scratch for a grouped forward (backward = 0) or backward (backward = 1):

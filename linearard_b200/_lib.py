@@ -54,9 +54,10 @@ class LKLGroupItem(ctypes.Structure):
     """One (relation, layer) item of a grouped call (struct lkl_group_item)."""
     _fields_ = [("qs", ctypes.c_void_p), ("ks", ctypes.c_void_p), ("qt", ctypes.c_void_p),
                 ("kt", ctypes.c_void_p), ("Hq", ctypes.c_int32), ("Hkv_s", ctypes.c_int32),
-                ("Hkv_t", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("Hkv_t", ctypes.c_int32), ("strided", ctypes.c_int32),
                 ("lse_s", ctypes.c_void_p), ("lse_t", ctypes.c_void_p),
-                ("dq", ctypes.c_void_p), ("dk", ctypes.c_void_p)]
+                ("dq", ctypes.c_void_p), ("dk", ctypes.c_void_p),
+                ("strides", LKLStrides * 4)]
 
 
 class LKLError(RuntimeError):

@@ -10,9 +10,12 @@ one dk launch per chunk of kv groups across items (``lkl_backward_grouped``).
 Loss values, LSEs and gradients are those of the per-item calls.
 
 Items share B, T, the head dims, dtypes, scales, causal flag and mask; each
-has its own head counts.  When an item is outside the tensor-core path
-(contiguous 16-byte-aligned inputs, Ds and Dt in {64, 128}, Hkv_s == Hkv_t)
-the call falls back to per-item ``attn_kl_align`` calls.
+has its own head counts.  Inputs may be [B, H, T, D] views with any strides
+that are multiples of 8 elements (the transposed projections an attention
+hook sees): they are read in place, as by ``attn_kl_align_strided``.  When an
+item is outside the tensor-core path (16-byte-aligned inputs, Ds and Dt in
+{64, 128}, Hkv_s == Hkv_t) the call falls back to per-item
+``attn_kl_align_strided`` calls.
 """
 from __future__ import annotations
 
@@ -21,23 +24,15 @@ import ctypes
 import torch
 
 from .. import _lib
-from ._common import check_pair, prepare_mask, problem, ptr, stream_of
-from .integration import attn_kl_align
+from ._common import prepare_mask, problem, ptr, stream_of
+from .strided import attn_kl_align_strided, strided_ok
 
 __all__ = ["attn_kl_align_grouped", "AttnKLAlignGroupedFn", "grouped_ok"]
 
 
 def grouped_ok(items) -> bool:
     """True when every item runs on the tensor-core path."""
-    for qs, ks, qt, kt in items:
-        for t in (qs, ks, qt, kt):
-            if not (t.is_cuda and t.is_contiguous() and t.data_ptr() % 16 == 0):
-                return False
-        if qs.shape[3] not in (64, 128) or qt.shape[3] not in (64, 128):
-            return False
-        if ks.shape[1] != kt.shape[1]:
-            return False
-    return True
+    return all(strided_ok(*it) for it in items)
 
 
 def _table(items, lse, grads=None):
@@ -45,7 +40,11 @@ def _table(items, lse, grads=None):
     for i, (qs, ks, qt, kt) in enumerate(items):
         e = arr[i]
         e.qs, e.ks, e.qt, e.kt = qs.data_ptr(), ks.data_ptr(), qt.data_ptr(), kt.data_ptr()
-        e.Hq, e.Hkv_s, e.Hkv_t, e.reserved = qs.shape[1], ks.shape[1], kt.shape[1], 0
+        e.Hq, e.Hkv_s, e.Hkv_t = qs.shape[1], ks.shape[1], kt.shape[1]
+        e.strided = 0 if all(t.is_contiguous() for t in (qs, ks, qt, kt)) else 1
+        if e.strided:
+            for k, t in enumerate((qs, ks, qt, kt)):
+                e.strides[k] = _lib.LKLStrides(b=t.stride(0), h=t.stride(1), t=t.stride(2))
         e.lse_s, e.lse_t = lse[i][0].data_ptr(), lse[i][1].data_ptr()
         if grads is not None:
             e.dq, e.dk = grads[i][0].data_ptr(), grads[i][1].data_ptr()
@@ -124,17 +123,27 @@ def attn_kl_align_grouped(items, attn_mask=None, causal=True, sm_scale_s=None,
     assert len(items) > 0, "items must not be empty"
     B, T = items[0][0].shape[0], items[0][0].shape[2]
     for qs, ks, qt, kt in items:
-        check_pair(qs, ks, "qs", "ks")
-        check_pair(qt, kt, "qt", "kt")
+        for name, t in (("qs", qs), ("ks", ks), ("qt", qt), ("kt", kt)):
+            assert isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor"
+            assert t.is_cuda, "Q/K must be on CUDA"
+            assert t.ndim == 4, f"{name} shape must be [B,H,T,D]"
+            assert t.stride(-1) == 1, f"{name} last-dim stride must be 1"
+        assert qs.dtype in (torch.float16, torch.bfloat16), "qs dtype supports only fp16/bf16"
+        assert qt.dtype in (torch.float16, torch.bfloat16), "qt dtype supports only fp16/bf16"
+        assert qs.dtype == ks.dtype and qt.dtype == kt.dtype, "q/k dtypes must match"
         assert tuple(qt.shape[:3]) == tuple(qs.shape[:3]), "student/teacher B/Hq/T must align"
+        assert (ks.shape[0], ks.shape[2], ks.shape[3]) == (qs.shape[0], qs.shape[2],
+                                                            qs.shape[3]), "qs/ks B/T/D must match"
+        assert qs.shape[1] % ks.shape[1] == 0 and qs.shape[1] % kt.shape[1] == 0, \
+            "Hq must be divisible by Hkv"
         assert (qs.shape[0], qs.shape[2]) == (B, T), "grouped items must share B and T"
         assert qs.shape[3] == items[0][0].shape[3] and qt.shape[3] == items[0][2].shape[3], \
             "grouped items must share the head dims"
         assert qs.dtype == items[0][0].dtype and qt.dtype == items[0][2].dtype, \
             "grouped items must share dtypes"
     if not grouped_ok(items):
-        return torch.stack([attn_kl_align(*it, attn_mask, causal, sm_scale_s, sm_scale_t)
-                            for it in items])
+        return torch.stack([attn_kl_align_strided(*it, attn_mask, causal, sm_scale_s,
+                                                  sm_scale_t) for it in items])
     flat = [t for it in items for t in it]
     return AttnKLAlignGroupedFn.apply(len(items), attn_mask, causal, sm_scale_s, sm_scale_t,
                                       *flat)

@@ -362,13 +362,16 @@ lkl_problem item_problem(const lkl_problem* shared, const lkl_group_item& it) {
   return q;
 }
 
-// Validation of a grouped call; fills `specs`.  backward: also the gradient rules.
+// Validation of a grouped call; fills `specs` (and `strides`, 4 per item).
+// backward: also the gradient rules.
 int32_t check_group(int32_t n, const lkl_group_item* items, const lkl_problem* shared,
-                    bool backward, std::vector<lkl::GroupSpec>& specs) {
+                    bool backward, std::vector<lkl::GroupSpec>& specs,
+                    std::vector<lkl::TensorStrides>& strides) {
   if (!items || !shared) return LKL_ERR_NULL_POINTER;
   if (n <= 0) return LKL_ERR_BAD_SHAPE;
   if (n > LKL_MAX_GROUP_ITEMS) return LKL_ERR_TOO_LARGE;
   specs.clear();
+  strides.assign((size_t)n * 4, lkl::TensorStrides{0, 0, 0});
   for (int i = 0; i < n; ++i) {
     const lkl_group_item& it = items[i];
     const lkl_problem q = item_problem(shared, it);
@@ -380,6 +383,16 @@ int32_t check_group(int32_t n, const lkl_group_item* items, const lkl_problem* s
     if (!lkl::sm100_shape_ok(pp) || !aligned(it.qs, 16) || !aligned(it.ks, 16) ||
         !aligned(it.qt, 16) || !aligned(it.kt, 16))
       return LKL_ERR_UNSUPPORTED;
+    if (it.strided != 0 && it.strided != 1) return LKL_ERR_BAD_SHAPE;
+    if (it.strided) {
+      const void* const ptrs[4] = {it.qs, it.ks, it.qt, it.kt};
+      if ((s = check_strides(it.strides, ptrs))) return s;
+      if (backward && it.dq == it.dk &&
+          (it.strides[0].b != it.strides[1].b || it.strides[0].h != it.strides[1].h ||
+           it.strides[0].t != it.strides[1].t))
+        return LKL_ERR_BAD_ALIAS;
+      to_strides(it.strides, &strides[(size_t)i * 4]);
+    }
     if (backward) {
       if (!it.dq || !it.dk) return LKL_ERR_NULL_POINTER;
       if (!aligned(it.dq, 16) || !aligned(it.dk, 16)) return LKL_ERR_MISALIGNED;
@@ -398,6 +411,7 @@ int32_t check_group(int32_t n, const lkl_group_item* items, const lkl_problem* s
     g.lse_t = it.lse_t;
     g.dq = it.dq;
     g.dk = it.dk;
+    g.strides = it.strided ? &strides[(size_t)i * 4] : nullptr;
     specs.push_back(g);
   }
   return LKL_OK;
@@ -432,7 +446,8 @@ size_t lkl_grouped_workspace_size(int32_t n, const lkl_group_item* items,
                                   const lkl_problem* shared, int32_t has_mask,
                                   int32_t backward) {
   std::vector<lkl::GroupSpec> specs;
-  if (check_group(n, items, shared, backward != 0, specs) != LKL_OK) return 0;
+  std::vector<lkl::TensorStrides> strides;
+  if (check_group(n, items, shared, backward != 0, specs, strides) != LKL_OK) return 0;
   if (shared->B <= 0 || shared->T <= 0) return 0;
   return group_layout(n, items, shared, has_mask != 0, backward != 0, specs).total;
 }
@@ -441,7 +456,8 @@ int32_t lkl_forward_grouped(int32_t n, const lkl_group_item* items, const void* 
                             const lkl_problem* shared, float* losses, void* ws, size_t ws_bytes,
                             void* stream) {
   std::vector<lkl::GroupSpec> specs;
-  int32_t s = check_group(n, items, shared, false, specs);
+  std::vector<lkl::TensorStrides> strides;
+  int32_t s = check_group(n, items, shared, false, specs, strides);
   if (s) return s;
   if (!losses) return LKL_ERR_NULL_POINTER;
   if (!aligned(losses, 4)) return LKL_ERR_MISALIGNED;
@@ -467,7 +483,8 @@ int32_t lkl_backward_grouped(int32_t n, const lkl_group_item* items, const void*
                              const lkl_problem* shared, const float* dlosses, void* ws,
                              size_t ws_bytes, void* stream) {
   std::vector<lkl::GroupSpec> specs;
-  int32_t s = check_group(n, items, shared, true, specs);
+  std::vector<lkl::TensorStrides> strides;
+  int32_t s = check_group(n, items, shared, true, specs, strides);
   if (s) return s;
   if (dlosses && !aligned(dlosses, 4)) return LKL_ERR_MISALIGNED;
   if ((s = check_mask(mask, shared->mask_dtype))) return s;

@@ -89,12 +89,14 @@ int sm100_num_partials(const Problem& p);
 // One item of a grouped call (relations / layers of one sequence): the
 // per-item tensors, head counts and outputs.  Items share B, T, the head
 // dims, dtypes, causal flag, scales and mask (the Problem passed beside them).
+struct TensorStrides;
 struct GroupSpec {
   const void *qs, *ks, *qt, *kt;
   int Hq, Hkv_s, Hkv_t;
-  float *lse_s, *lse_t;  // forward outputs, backward inputs
-  float *dq, *dk;        // backward outputs; dq == dk = fused (qs == ks)
-  const float* dloss;    // backward: device scalar or nullptr (= 1)
+  float *lse_s, *lse_t;          // forward outputs, backward inputs
+  float *dq, *dk;                // backward outputs; dq == dk = fused (qs == ks)
+  const float* dloss;            // backward: device scalar or nullptr (= 1)
+  const TensorStrides* strides;  // qs, ks, qt, kt strides, or nullptr (contiguous)
 };
 
 // Element strides of a [B][H][T][D] input (the d stride is 1).

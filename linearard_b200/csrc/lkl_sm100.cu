@@ -1296,7 +1296,7 @@ bool build_group(const Problem& base, const GroupSpec* g, int n, std::vector<uin
     p.Hkv_s = g[i].Hkv_s;
     p.Hkv_t = g[i].Hkv_t;
     Maps m;
-    if (!build_maps(m, p, g[i].qs, g[i].ks, g[i].qt, g[i].kt, nullptr)) return false;
+    if (!build_maps(m, p, g[i].qs, g[i].ks, g[i].qt, g[i].kt, g[i].strides)) return false;
     GroupItem& it = items[i];
     it.qs = m.qs;
     it.ks = m.ks;

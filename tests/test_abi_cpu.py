@@ -27,7 +27,7 @@ def test_library_loads_and_exports_header_symbols():
     assert set(names) == set(_lib.EXPORTS)
     for n in names:
         assert hasattr(L, n), n
-    assert L.lkl_abi_version() == 4
+    assert L.lkl_abi_version() == 5
 
 
 def test_status_strings():

@@ -83,6 +83,34 @@ def test_masked_noncausal_d64_fp16():
     _check(_items(2, B, T, 64, specs, torch.float16), mask=mask.cuda(), causal=False)
 
 
+def test_strided_items_transposed_projections():
+    """Items given as [B, H, T, D] views of [B, T, H, D] projections (what an
+    attention hook sees) are read in place: same results as contiguous items."""
+    B, T, D = 1, 520, 128
+    g = torch.Generator().manual_seed(6)
+    items = []
+    for H in (4, 2, 2):
+        xs = _t(g, B, T, H, D)
+        xt = (xs.float() + 0.3 * _t(g, B, T, H, D, dtype=torch.float32)).to(torch.bfloat16)
+        items.append((xs.transpose(1, 2), xs.transpose(1, 2), xt.transpose(1, 2),
+                      xt.transpose(1, 2)))
+    a = []
+    for qs, _, qt, _ in items:
+        leaf = qs.detach().transpose(1, 2).clone().transpose(1, 2).requires_grad_(True)
+        assert not leaf.is_contiguous()
+        a.append((leaf, leaf, qt, qt))
+    losses = attn_kl_align_grouped(a)
+    losses.sum().backward()
+    b = [(qs.detach().contiguous().requires_grad_(True), qt.contiguous()) for qs, _, qt, _ in items]
+    ref = attn_kl_align_grouped([(q, q, t, t) for q, t in b])
+    ref.sum().backward()
+    torch.cuda.synchronize()
+    check_device_status()
+    assert torch.equal(losses.detach(), ref.detach())
+    for (q, _, _, _), (qr, _) in zip(a, b):
+        assert torch.equal(q.grad, qr.grad)
+
+
 def test_items_outside_the_tensor_core_path_fall_back_per_item():
     specs = [(2, 2, True)]
     items = _items(4, 1, 200, 32, specs)
