@@ -1138,10 +1138,10 @@ cudaError_t run_grad(const Problem& p, const Maps& m, const std::vector<Chunk>& 
 constexpr long long kDTileBytes = (long long)kDTileElems * 2;
 
 // kv groups per band of dk work items: the bands' Qs tiles (G heads of T rows
-// each) stay within a quarter of the 126 MB L2.
+// each) stay within half of the 126 MB L2.
 int dk_band(const Problem& p, int G) {
   const long long per_group = (long long)G * p.T * p.Ds * 2;
-  return (int)std::max<long long>(1, (32ll << 20) / std::max<long long>(per_group, 1));
+  return (int)std::max<long long>(1, (64ll << 20) / std::max<long long>(per_group, 1));
 }
 
 long long d_tiles_per_head(const Problem& p) {
