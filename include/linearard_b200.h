@@ -186,7 +186,9 @@ int32_t lkl_backward_strided(const void* qs, const void* ks, const float* lse_s,
  * The item table (tensor maps and pointers, 576 B per item) goes to the device
  * inside the call through a pinned host ring that the library allocates once
  * (8 MiB, the only host allocation it makes), so the call does not wait for
- * the stream.
+ * the stream.  Because the table is read from that ring when the copy runs,
+ * grouped calls must not be captured into CUDA graphs (the single-problem
+ * entry points have no such restriction).
  * Results equal the per-item calls: lkl_forward_grouped writes each item's
  * lse_s, lse_t and losses[i] (device fp32 [n], the row-KL sum of item i);
  * lkl_backward_grouped reads them and writes each item's dq and dk (dq == dk:
