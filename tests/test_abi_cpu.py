@@ -27,7 +27,9 @@ def test_library_loads_and_exports_header_symbols():
     assert set(names) == set(_lib.EXPORTS)
     for n in names:
         assert hasattr(L, n), n
-    assert L.lkl_abi_version() == 5
+    # the version build() checks: the header's LKL_ABI_VERSION
+    want = int(re.search(r"#define LKL_ABI_VERSION (\d+)", open(HEADER).read()).group(1))
+    assert L.lkl_abi_version() == want
 
 
 def test_status_strings():
