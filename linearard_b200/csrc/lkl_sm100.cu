@@ -1,8 +1,8 @@
 // sm_100a tensor-core kernels for the attention-relation KL loss.
 //
-// Both kernels are row-stationary: one CTA owns a 128-row tile i of one
-// (batch, query head) and walks the 128-column tiles j <= i (all j when not
-// causal).  Operand tiles are staged by TMA (128-byte swizzle, no multicast),
+// The forward and dq kernels are row-stationary: one CTA owns a 128-row tile
+// i of one (batch, query head) and walks the 128-column tiles j <= i (all j
+// when not causal); the dk kernel is a persistent GEMM over the D tiles.  Operand tiles are staged by TMA (128-byte swizzle, no multicast),
 // scores are computed by tcgen05.mma into TMEM, and sixteen "row" warps (four
 // warpgroups, each owning 32 of the 128 columns of a tile for all 128 rows)
 // read them back with tcgen05.ld.
@@ -471,23 +471,18 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs0,
 }
 
 // ============================================================== backward
-// The gradient is computed by two reduction-free launches of one kernel:
-//   DK = false: row-stationary (query tile i, key tiles j <= i):
-//               dq_i = sc * sum_j D_ij Ks_j
-//   DK = true : column-stationary (key tile j, query tiles i >= j of every
-//               query head of its kv group): dk_j = sc * sum_i D_ij Qs_i
-// Both recompute the scores of their tile pairs and D = e^{ss - lse_s} -
-// e^{st - lse_t}, rounded to the input dtype (kernel_C.py:224-233).  Each
-// output row is owned by exactly one CTA and written once, so no fp32
-// partials go through L2 reductions and the gradients are reproducible bit
-// for bit (the reference adds dk with float atomics, kernel_C.py:242-253).
-// The price is computing the scores and exponentials of each tile pair twice.
-//
-// The two variants run the same MMA sequence: the stationary operand tile
-// (Q for dq, K for dk) is A of the score GEMMs, the streamed tile is B, and
-// the gradient GEMM multiplies D (or D^T) from shared memory by the streamed
-// tile's student half read as an MN-major operand.  For dk the TMEM scores
-// are transposed (lane = key j, column = query i).
+// The gradient takes two reduction-free launches per chunk of the D buffer:
+//   dq launch (row-stationary: query tile i, key tiles j <= i):
+//     recompute ss, st; D = e^{ss - lse_s} - e^{st - lse_t} rounded to the
+//     input dtype (kernel_C.py:224-233); dq_i = sc * sum_j D_ij Ks_j; D
+//     stored to HBM;
+//   dk launch (persistent GEMM over (kv head, key tile j)):
+//     dk_j = sc * sum_i D_ij^T Qs_i, reading the stored D tiles.
+// Each output row is owned by one CTA per chunk and written once (later
+// chunks add in a fixed order), so no fp32 partials go through L2 reductions
+// and the gradients are reproducible bit for bit (the reference adds dk with
+// float atomics, kernel_C.py:242-253).  Exponentials are computed once per
+// tile pair; the D hand-off costs 32 KB of HBM writes and reads per pair.
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2t(float a, float b) {
   if (BF16) {
