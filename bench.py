@@ -27,6 +27,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 E2E_SLICE = 8      # heads per host->device slice in the end-to-end measurement
+E2E_FIRST = 2      # heads of the first slice (the one copy not hidden under compute)
 METRIC = "KL fwd+bwd tokens/s, LLaMA3-8B heads @32K ctx; % bf16 tensor peak"
 WORKLOAD = "llama3_8b_32k"
 
@@ -341,10 +342,15 @@ def main():
         # the start of the step; the forward of slice k waits only for slice k's
         # copy, so the PCIe transfer of later slices runs under earlier compute.
         slices = []
-        for r in cfg.relations:
+        for ri, r in enumerate(cfg.relations):
             H = students[r].shape[1]
-            for h0 in range(0, H, E2E_SLICE):
-                h1 = min(H, h0 + E2E_SLICE)
+            # slice boundaries: E2E_SLICE heads each, except that the first
+            # slice of the step is E2E_FIRST heads (its copy is the one that
+            # nothing hides)
+            bounds = list(range(0, H, E2E_SLICE)) + [H]
+            if ri == 0 and E2E_FIRST < min(H, E2E_SLICE):
+                bounds = [0, E2E_FIRST] + bounds[1:]
+            for h0, h1 in zip(bounds[:-1], bounds[1:]):
                 hs = students[r].detach()[:, h0:h1].contiguous().cpu().pin_memory()
                 ht = teachers[r][:, h0:h1].contiguous().cpu().pin_memory()
                 slices.append((hs, ht, torch.empty_like(hs, device=dev),
