@@ -126,6 +126,30 @@ def test_chunked_backward_matches_one_chunk(case):
         assert_grad_close(ref_dk.numpy(), dk_o, "dk")
 
 
+def test_chunked_backward_gqa4_with_padding_mask():
+    """Four query heads per kv head and a padding mask, with workspaces from
+    the whole D buffer down to one query-tile row of a kv group."""
+    B, Hq, Hkv, T, D = 2, 8, 2, 520, 128
+    args = _inputs(11, B, Hq, Hkv, T, D, False)
+    g = torch.Generator().manual_seed(12)
+    mask = (torch.rand(B, T, generator=g) > 0.25).to(torch.int32)
+    mask[:, 0] = 1
+    mask = mask.cuda()
+    prob = _problem(B, Hq, Hkv, T, D, True)
+    n_t = math.ceil(T / 128)
+    ref_dq, ref_dk, lse_s, lse_t = _run(args, prob, None, False, mask)
+    for tiles in (2 * 4 * _tiles(T, True), 4 * _tiles(T, True), 4 * n_t):
+        dq, dk, _, _ = _run(args, prob, tiles, False, mask)
+        torch.testing.assert_close(dq, ref_dq, rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(dk, ref_dk, rtol=1e-5, atol=1e-6)
+    qs, ks, qt, kt = (C.float().numpy().astype(np.float64) for C in args)
+    sc = 1.0 / math.sqrt(D)
+    dq_o, dk_o = O.oracle_grad(qs, ks, lse_s.numpy(), qt, kt, lse_t.numpy(), mask.cpu().numpy(),
+                               True, sc, sc)
+    assert_grad_close(ref_dq.numpy(), dq_o, "dq")
+    assert_grad_close(ref_dk.numpy(), dk_o, "dk")
+
+
 def test_backward_refuses_less_than_one_row_of_tiles():
     L = _lib.lib()
     B, Hq, Hkv, T, D = 1, 4, 2, 1300, 128
