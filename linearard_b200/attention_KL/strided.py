@@ -12,8 +12,8 @@ are: the tensor-core kernels read them in place through 4-D TMA maps
 Same value, gradients and call signature as ``attn_kl_align``.  Inputs need a
 last-dim stride of 1, the other strides multiples of 8 elements and 16-byte
 aligned storage; shapes the tensor-core path does not cover (Ds or Dt not in
-{64, 128}, Hkv_s != Hkv_t, other strides) go through ``attn_kl_align`` on
-contiguous copies, i.e. the same GPU kernels the reference-shaped call uses.
+{64, 128}, other strides) go through ``attn_kl_align`` on contiguous copies,
+i.e. the same GPU kernels the reference-shaped call uses.
 """
 from __future__ import annotations
 
@@ -44,7 +44,7 @@ def strided_ok(qs, ks, qt, kt) -> bool:
                                                                             torch.bfloat16):
         return False
     return (qs.shape[3] in (64, 128) and qt.shape[3] in (64, 128)
-            and ks.shape[1] == kt.shape[1] and qs.shape[1] % ks.shape[1] == 0)
+            and qs.shape[1] % ks.shape[1] == 0 and qs.shape[1] % kt.shape[1] == 0)
 
 
 def _array(*ts):

@@ -170,8 +170,8 @@ const char* lkl_status_string(int32_t s) {
     case LKL_ERR_BAD_ALIAS: return "dq == dk requires qs == ks and Hkv_s == Hq";
     case LKL_ERR_TOO_LARGE: return "problem exceeds the supported size";
     case LKL_ERR_UNSUPPORTED:
-      return "strided inputs need the tensor-core path (sm_100, Ds and Dt in {64, 128}, "
-             "16-byte aligned; Hkv_s == Hkv_t for the backward)";
+      return "strided or grouped inputs need the tensor-core path (sm_100, Ds and Dt in "
+             "{64, 128}, 16-byte aligned)";
     default: return "unknown status";
   }
 }
@@ -397,7 +397,6 @@ int32_t check_group(int32_t n, const lkl_group_item* items, const lkl_problem* s
       if (!it.dq || !it.dk) return LKL_ERR_NULL_POINTER;
       if (!aligned(it.dq, 16) || !aligned(it.dk, 16)) return LKL_ERR_MISALIGNED;
       if (it.dq == it.dk && (it.qs != it.ks || it.Hkv_s != it.Hq)) return LKL_ERR_BAD_ALIAS;
-      if (it.Hkv_s != it.Hkv_t) return LKL_ERR_UNSUPPORTED;
     }
     lkl::GroupSpec g{};
     g.qs = it.qs;

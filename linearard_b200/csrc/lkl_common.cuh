@@ -110,8 +110,8 @@ cudaError_t launch_sm100_forward(const Problem& p, const void* qs, const void* k
                                  const uint32_t* bits, float* lse_s, float* lse_t,
                                  float* partials, int* num_partials, cudaStream_t st);
 // Backward: per chunk, a dq launch that also stores the rounded D tiles into
-// `dbuf`, then a dk GEMM launch over them; no reductions.  Needs Hkv_s ==
-// Hkv_t.  `lsc` is B*Hq*T float2 of scratch, `dbuf` at least
+// `dbuf`, then a dk GEMM launch over them; no reductions.  `lsc` is B*Hq*T
+// float2 of scratch, `dbuf` at least
 // sm100_dbuf_bytes(p) bytes (smaller buffers give more, smaller chunks; too
 // small for one query-tile row of a kv group -> cudaErrorInvalidValue).
 bool sm100_backward_supports(const Problem& p);

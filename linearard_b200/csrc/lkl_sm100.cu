@@ -1377,11 +1377,13 @@ cudaError_t launch_sm100_forward(const Problem& p, const void* qs, const void* k
 }
 
 bool sm100_backward_supports(const Problem& p) {
-  return sm100_supports(p) && p.Hkv_s == p.Hkv_t;
+  // the teacher's kv grouping only enters the dq launch (its score GEMM);
+  // D and the dk launch depend on the student's grouping alone
+  return sm100_supports(p);
 }
 
 size_t sm100_dbuf_bytes(const Problem& p) {
-  if (p.B <= 0 || p.T <= 0 || !sm100_shape_ok(p) || p.Hkv_s != p.Hkv_t) return 0;
+  if (p.B <= 0 || p.T <= 0 || !sm100_shape_ok(p)) return 0;
   const long long all = (long long)p.B * p.Hq * d_tiles_per_head(p);
   const long long cap = kDBufCapBytes / kDTileBytes;
   const long long row = (long long)(p.Hq / p.Hkv_s) * ((p.T + kBM - 1) / kBM);

@@ -63,7 +63,7 @@ def test_backward_workspace_holds_the_d_tiles():
     beyond 8 GiB the buffer is capped and the backward runs in chunks."""
     L = _lib.lib()
     for mask in (0, 1):
-        p = _prob(Hkv_t=2)                      # Hkv_s == Hkv_t: tensor-core backward
+        p = _prob(Hkv_t=2)                      # tensor-core backward
         base = L.lkl_workspace_size(ctypes.byref(p), mask)
         n_t = (300 + 127) // 128
         tiles = 1 * 4 * n_t * (n_t + 1) // 2    # causal: tiles j <= i per head
@@ -72,10 +72,14 @@ def test_backward_workspace_holds_the_d_tiles():
         assert (L.lkl_backward_workspace_size(ctypes.byref(nc), mask)
                 == L.lkl_workspace_size(ctypes.byref(nc), mask) + 4 * n_t * n_t * 32768)
     # shapes served by the CUDA-core kernels need nothing extra
-    for kw in (dict(), dict(Ds=32, Dt=32, Hkv_t=2)):   # Hkv_s != Hkv_t; head dim 32
+    for kw in (dict(Ds=32, Dt=32, Hkv_t=2), dict(Ds=256, Dt=128)):   # head dims 32 and 256
         p = _prob(**kw)
         assert (L.lkl_backward_workspace_size(ctypes.byref(p), 0)
                 == L.lkl_workspace_size(ctypes.byref(p), 0))
+    # different student / teacher kv-head counts: tensor-core backward as well
+    asym = _prob()                                      # Hkv_s 2, Hkv_t 4
+    assert (L.lkl_backward_workspace_size(ctypes.byref(asym), 0)
+            == L.lkl_workspace_size(ctypes.byref(asym), 0) + 4 * n_t * (n_t + 1) // 2 * 32768)
     # LLaMA3-8B Q/Q relation at 32K: 32 heads x 32896 tiles -> capped at 8 GiB
     big = _prob(B=1, Hq=32, Hkv_s=32, Hkv_t=32, T=32768)
     extra = (L.lkl_backward_workspace_size(ctypes.byref(big), 0)
@@ -218,10 +222,11 @@ def test_grouped_entry_points_validate_before_device():
     bad = (_lib.LKLGroupItem * 1)(item(dq=fake, dk=fake))
     assert L.lkl_backward_grouped(1, bad, None, ctypes.byref(shared), None, c(fake), 1 << 20,
                                   None) == 10
-    # Hkv_s != Hkv_t: no tensor-core backward
+    # Hkv_s != Hkv_t is on the tensor-core path: this one fails later, on the
+    # workspace (16 bytes)
     mixed = (_lib.LKLGroupItem * 1)(item(Hkv_t=4))
-    assert L.lkl_backward_grouped(1, mixed, None, ctypes.byref(shared), None, c(fake), 1 << 20,
-                                  None) == 12
+    assert L.lkl_backward_grouped(1, mixed, None, ctypes.byref(shared), None, c(fake), 16,
+                                  None) == 6
     assert L.lkl_forward_grouped(0, one, None, ctypes.byref(shared), c(fake), c(fake), 1 << 20,
                                  None) == 2
     assert L.lkl_forward_grouped(1, one, None, ctypes.byref(shared), c(fake), c(fake), 16,

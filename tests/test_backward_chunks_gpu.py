@@ -150,6 +150,33 @@ def test_chunked_backward_gqa4_with_padding_mask():
     assert_grad_close(ref_dk.numpy(), dk_o, "dk")
 
 
+def test_tensor_core_backward_with_different_kv_head_counts():
+    """Student kv heads 2, teacher kv heads 4 (Hq 8): the tensor-core backward
+    (the teacher grouping enters only the dq launch's teacher scores), whole
+    and chunked, against the oracle."""
+    L = _lib.lib()
+    B, Hq, Hkv_s, Hkv_t, T, D = 1, 8, 2, 4, 400, 64
+    g = torch.Generator().manual_seed(21)
+    qs = torch.randn(B, Hq, T, D, generator=g).bfloat16()
+    ks = torch.randn(B, Hkv_s, T, D, generator=g).bfloat16()
+    qt = (qs.float() + 0.3 * torch.randn(B, Hq, T, D, generator=g)).bfloat16()
+    kt = torch.randn(B, Hkv_t, T, D, generator=g).bfloat16()
+    prob = _lib.LKLProblem(B=B, Hq=Hq, Hkv_s=Hkv_s, Hkv_t=Hkv_t, T=T, Ds=D, Dt=D,
+                           dtype_s=_lib.LKL_BF16, dtype_t=_lib.LKL_BF16, causal=1,
+                           mask_dtype=_lib.LKL_MASK_I32, sm_scale_s=0.0, sm_scale_t=0.0)
+    args = (qs, ks, qt, kt)
+    ref_dq, ref_dk, lse_s, lse_t = _run(args, prob, None, False)
+    dq, dk, _, _ = _run(args, prob, (Hq // Hkv_s) * math.ceil(T / 128), False)
+    torch.testing.assert_close(dq, ref_dq, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(dk, ref_dk, rtol=1e-5, atol=1e-6)
+    a = [x.float().numpy().astype(np.float64) for x in args]
+    sc = 1.0 / math.sqrt(D)
+    dq_o, dk_o = O.oracle_grad(a[0], a[1], lse_s.numpy(), a[2], a[3], lse_t.numpy(), None, True,
+                               sc, sc)
+    assert_grad_close(ref_dq.numpy(), dq_o, "dq")
+    assert_grad_close(ref_dk.numpy(), dk_o, "dk")
+
+
 def test_backward_refuses_less_than_one_row_of_tiles():
     L = _lib.lib()
     B, Hq, Hkv, T, D = 1, 4, 2, 1300, 128

@@ -50,8 +50,8 @@ def test_forward_backward_match_reference(case, generic, golden):
     torch.cuda.synchronize()
     check_device_status()
     expect_tc = (not generic) and case.Ds in TC_DIMS and case.Dt in TC_DIMS
-    # the tensor-core backward needs the same kv-head count for student and teacher
-    assert used_tc == expect_tc and used_tc_b == (expect_tc and case.Hkv_s == case.Hkv_t)
+    # the tensor-core backward covers different student / teacher kv-head counts too
+    assert used_tc == expect_tc and used_tc_b == expect_tc
     torch.testing.assert_close(lse_s.cpu(), torch.from_numpy(g["lse_s"]), rtol=rtol, atol=atol)
     torch.testing.assert_close(lse_t.cpu(), torch.from_numpy(g["lse_t"]), rtol=rtol, atol=atol)
     assert_loss_close(float(loss), float(g["kl"]))
