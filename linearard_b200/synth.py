@@ -15,8 +15,7 @@ Everything is generated with explicit ``torch.Generator`` objects so that a
 """
 from __future__ import annotations
 
-import math
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import torch
 

@@ -1,6 +1,5 @@
 """Shared helpers for the GPU parity tests."""
 import numpy as np
-import torch
 
 from linearard_b200 import _lib
 

@@ -9,7 +9,6 @@ import pytest
 import torch
 
 from linearard_b200 import _lib
-from linearard_b200.attention_KL import _common
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 HEADER = os.path.join(ROOT, "include", "linearard_b200.h")

@@ -2,7 +2,6 @@
 LLaMA size: its loss and LoRA gradients against the reference's materialised
 PyTorch formulation of the same loss (``integration.py:102-127``, fp32) on
 the same captured q/k/v, normalised as ``train.py:380-410``."""
-import argparse
 
 import pytest
 import torch

@@ -4,7 +4,6 @@ by the oracle on each rank's shard) equal the single-process total."""
 import os
 import socket
 
-import numpy as np
 import pytest
 import torch
 import torch.distributed as dist
