@@ -180,3 +180,35 @@ def test_small_d_buffer_chunks_across_items():
         else:
             assert torch.equal(q.grad.float(), outs[0][i][0].to(q.grad.dtype).float())
             assert torch.equal(k.grad.float(), outs[0][i][1].to(k.grad.dtype).float())
+
+
+def test_grouped_mixed_items_masked_noncausal():
+    """Contiguous and strided items together, different student / teacher kv
+    heads, a padding mask, non-causal: bitwise the per-item calls."""
+    B, T, D = 2, 400, 128
+    g = torch.Generator().manual_seed(41)
+    mask = (torch.rand(B, T, generator=g) > 0.25).to(torch.bool)
+    mask[:, 0] = True
+    items = _items(42, B, T, D, [(4, 4, True), (4, 2, False)])
+    # a strided item: [B, T, H, D] memory
+    xs = _t(g, B, T, 4, D)
+    xt = (xs.float() + 0.3 * _t(g, B, T, 4, D, dtype=torch.float32)).to(torch.bfloat16)
+    ks = _t(g, B, T, 2, D)
+    kt = _t(g, B, T, 1, D)
+    items.append((xs.transpose(1, 2), ks.transpose(1, 2), xt.transpose(1, 2), kt.transpose(1, 2)))
+    a = _leaves(items)
+    losses = attn_kl_align_grouped(a, attn_mask=mask.cuda(), causal=False)
+    assert path_is_tensor_core()
+    losses.sum().backward()
+    b = _leaves(items)
+    from linearard_b200.attention_KL import attn_kl_align_strided
+    ref = torch.stack([attn_kl_align_strided(*it, attn_mask=mask.cuda(), causal=False)
+                       for it in b])
+    ref.sum().backward()
+    torch.cuda.synchronize()
+    check_device_status()
+    assert torch.equal(losses.detach(), ref.detach())
+    for ga, gb in zip(_grads(a), _grads(b)):
+        assert torch.equal(ga[0], gb[0])
+        if gb[1] is not None:
+            assert torch.equal(ga[1], gb[1])
