@@ -1,6 +1,6 @@
 """Summarise ncu CSV output for the profiles/ notes.
 
-    python -m linearard_b200.ncu_summary launches gpurun_out/launches.csv
+    python -m linearard_b200.ncu_summary launches launches.csv
         per kernel: launches, total gpu__time_duration, share of the total
     python -m linearard_b200.ncu_summary raw report.csv
         selected raw metrics (``ncu -i x.ncu-rep --page raw --csv``) per kernel

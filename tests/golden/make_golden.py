@@ -74,7 +74,9 @@ def _compact(a: np.ndarray) -> np.ndarray:
 
 
 def main():
-    root = os.environ.get("LINEARARD_REF", "/root/reference")
+    root = os.environ.get("LINEARARD_REF")
+    if not root:
+        raise SystemExit("set LINEARARD_REF to a LinearARD checkout (see the module docstring)")
     reference_lse, reference_kl, reference_grad = _import_reference(root)
     out = {}
     torch.set_num_threads(max(1, os.cpu_count() or 1))
