@@ -3,8 +3,8 @@
 One step = the Q/Q (32 heads), K/K (8 heads) and V/V (8 heads) relation losses of
 one layer for one sequence (n = 32768, d = 128, bf16, causal), forward and
 backward through the public ``attn_kl_align`` operator, plus the scalar-loss
-all-reduce over NCCL when N > 1.  Each rank owns one sequence (weak scaling;
-BASELINE config 4's "one sequence per GPU").
+all-reduce over NCCL when N > 1.  Each rank owns one sequence (weak scaling,
+one sequence per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 

@@ -1,7 +1,7 @@
 """End-to-end self-distillation step with the KL operator dropped in.
 
 This is the training step of LinearARD's ``train.py:165-465`` for the
-configuration BASELINE config 5 names: a random-init LLaMA2-7B architecture
+end-to-end benchmark configuration: a random-init LLaMA2-7B architecture
 (32 layers, hidden 4096, 32 heads, d = 128, vocab 32000), uniform random
 token ids, seq 16384, batch 1 per GPU; a frozen teacher with native RoPE and
 a student with linear-scaled RoPE (factor 8) and LoRA r = 16 on q/k/v; the

@@ -59,7 +59,7 @@ class RelationConfig:
 
 
 CONFIGS = {
-    # CPU reference check (fp32, one Q/Q head)
+    # the CPU reference check: fp32, one Q/Q head
     "cfg1_cpu_check": RelationConfig("cfg1_cpu_check", 1, 1, 1, 64, 512, 1.0e4,
                                      relations=("q",), dtype=torch.float32),
     # LLaMA2-7B head shape

@@ -13,7 +13,7 @@ checkout and calls their materialised PyTorch oracles on CPU tensors:
 * ``reference_kl``   (test_kernel_B.py:63-106), fed with ``reference_lse``
 * ``reference_grad`` (test_kernel_C.py:64-117), fed with ``reference_lse``
 
-and, for BASELINE config 1 (one Q/Q head, n=512, d=64, fp32, RoPE theta=1e4,
+and, for the CPU-check configuration (one Q/Q head, n=512, d=64, fp32, RoPE theta=1e4,
 student at positions/8), the loss and its autograd gradient through the
 materialised softmax formulation of ``kernels/attention_KL/integration.py:102-127``.
 
@@ -101,7 +101,7 @@ def main():
         out[f"{c.name}/dq"] = _compact(dq.float().numpy())
         out[f"{c.name}/dk"] = _compact(dk.float().numpy())
 
-    # Q/Q relation, fp32, n=512, d=64, causal, RoPE.
+    # the CPU-check configuration: Q/Q relation, fp32, n=512, d=64, causal, RoPE.
     cfg = CONFIGS["cfg1_cpu_check"]
     student, teacher = make_relations(cfg, device="cpu")["q"]
     sc = C.sm_scale(cfg.head_dim)

@@ -1,6 +1,6 @@
 """AttnKLAlignFn / attn_kl_align end to end on a B200 (autograd included),
-against the numpy oracle and LinearARD's golden config-1 values, plus
-size-independent properties at BASELINE sizes."""
+against the numpy oracle and LinearARD's golden CPU-check values, plus
+size-independent properties at the benchmark sizes."""
 import numpy as np
 import pytest
 import torch
@@ -44,7 +44,7 @@ def test_attn_kl_align_autograd_vs_oracle(shared, D):
 
 
 def test_cfg1_against_reference_golden(golden):
-    """BASELINE config 1 (one Q/Q head, n=512, d=64, RoPE, student at pos/8).
+    """The CPU-check configuration (one Q/Q head, n=512, d=64, RoPE, student at pos/8).
     The reference computes it in fp32; the kernels take fp16 inputs, so the
     comparison is tight against the oracle on the rounded inputs and loose
     against the fp32 golden."""

@@ -43,7 +43,7 @@ def test_oracle_cfg1_matches_reference_and_autograd(golden):
     loss, lse_s, lse_t = O.oracle_attn_kl_align(s, s, t, t)
     assert abs(loss - float(golden["cfg1/kl"])) < 1e-4
     assert abs(loss - float(golden["cfg1/loss_autograd"])) < 1e-4
-    # mean over rows, as BASELINE config 1 states it
+    # mean over rows, as the CPU-check configuration states it
     assert abs(loss / cfg.seq_len - 0.087692) < 1e-6
     dq, dk = O.oracle_attn_kl_align_backward(s, s, t, t)
     g = dq + dk

@@ -17,7 +17,7 @@ import torch
 
 from linearard_b200 import _lib
 
-LOSS_REL = 1e-3   # north-star loss tolerance used by every parity test
+LOSS_REL = 1e-3   # loss tolerance used by every parity test
 LSE_TOL = 1e-4
 
 
