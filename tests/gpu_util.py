@@ -35,13 +35,13 @@ def grad_metrics(got, ref):
 
 
 def assert_grad_close(got, ref, name="grad", cos_min=0.999, rel_max=2e-2):
-    """North-star gradient bar: cosine >= 0.999 and max|a-b|/max|b| <= 2e-2."""
+    """Parity bar for gradients: cosine >= 0.999 and max|a-b|/max|b| <= 2e-2."""
     cos, rel = grad_metrics(got, ref)
     assert cos >= cos_min and rel <= rel_max, f"{name}: cosine {cos:.6f}, max rel err {rel:.3e}"
 
 
 def assert_loss_close(got, ref, rel=1e-3, abs_=1e-3, name="loss"):
-    """North-star loss bar: relative error <= 1e-3 (plus a small absolute floor
+    """Parity bar for losses: relative error <= 1e-3 (plus a small absolute floor
     for near-zero sums)."""
     assert abs(got - ref) <= rel * abs(ref) + abs_, f"{name}: {got} vs {ref}"
 
