@@ -54,18 +54,21 @@ def load_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def backward_chunks(heads: int, group: int, T: int, causal: bool) -> int:
-    """Chunks the tensor-core backward splits a relation into when given
-    lkl_backward_workspace_size bytes (D tiles of 32 KB, at most 8 GiB of
-    them, whole kv groups per chunk; a restatement of the library's plan for
-    the shapes this benchmark runs)."""
-    n_t = -(-T // 128)
-    per_head = n_t * (n_t + 1) // 2 if causal else n_t * n_t
-    cap = max(min(heads * per_head, (8 << 30) // 32768), group * n_t)
-    groups = heads // group
-    per = min(groups, cap // (group * per_head))
-    assert per >= 1, "row-split plans are not counted here"
-    return -(-groups // per)
+def backward_chunks(t: "torch.Tensor", causal: bool) -> int:
+    """Chunks (one dq and one dk launch each) of the fused backward of the
+    symmetric call on `t` [B, H, T, D], with lkl_backward_workspace_size bytes
+    of scratch, as the library plans them (lkl_backward_plan)."""
+    import ctypes
+
+    from linearard_b200 import _lib
+    from linearard_b200.attention_KL._common import problem
+    prob = problem(t, t, t, t, causal, _lib.LKL_MASK_U8, None, None)
+    L = _lib.lib()
+    ws = L.lkl_backward_workspace_size(ctypes.byref(prob), 0)
+    n = ctypes.c_int32(0)
+    _lib.check(L.lkl_backward_plan(ctypes.byref(prob), 0, ws, 1, ctypes.byref(n)),
+               "lkl_backward_plan")
+    return n.value
 
 
 # ------------------------------------------------------------------ CPU side
@@ -295,8 +298,7 @@ def main():
     assert st == 0, f"device status {st}"
     # per relation: forward kernel + loss reduction; backward: lse pre-pass, then
     # a dq and a dk launch per chunk of the D-tile buffer
-    launches_per_step = sum(3 + 2 * backward_chunks(students[r].shape[1], 1, cfg.seq_len,
-                                                    cfg.causal)
+    launches_per_step = sum(3 + 2 * backward_chunks(students[r].detach(), cfg.causal)
                             for r in cfg.relations)
 
     # ---- per-kernel timing of the dominant kernels (same stream, CUDA events)

@@ -223,6 +223,14 @@ int32_t lkl_backward_grouped(int32_t n, const lkl_group_item* items, const void*
                              const lkl_problem* shared, const float* dlosses, void* workspace,
                              size_t workspace_bytes, void* stream);
 
+/* Host-only query (no device work): how many chunks (one dq and one dk launch
+ * each) lkl_backward splits problem `p` into with `workspace_bytes` of scratch
+ * (fused != 0: dq == dk).  *n_chunks = 0 for shapes the CUDA-core kernels
+ * serve (one launch, no D buffer).  LKL_ERR_WORKSPACE below the minimum.
+ * Added in ABI version 5. */
+int32_t lkl_backward_plan(const lkl_problem* p, int32_t has_mask, size_t workspace_bytes,
+                          int32_t fused, int32_t* n_chunks);
+
 /* Device-side error word of the current device: the bounded waits inside the
  * tensor-core kernels set it instead of hanging.  Reads (synchronously) and
  * clears it; returns LKL_OK or LKL_ERR_DEVICE_TIMEOUT. */

@@ -32,7 +32,7 @@ EXPORTS = ("lkl_abi_version", "lkl_status_string", "lkl_workspace_size", "lkl_ls
            "lkl_last_path", "lkl_set_force_generic", "lkl_forward_noalloc",
            "lkl_last_cuda_error", "lkl_backward_workspace_size", "lkl_forward_strided",
            "lkl_backward_strided", "lkl_grouped_workspace_size", "lkl_forward_grouped",
-           "lkl_backward_grouped")
+           "lkl_backward_grouped", "lkl_backward_plan")
 
 
 class LKLProblem(ctypes.Structure):
@@ -111,6 +111,8 @@ def _declare(L):
     L.lkl_forward_grouped.argtypes = [_i32, _G, _vp, _P, _vp, _vp, _sz, _vp]
     L.lkl_backward_grouped.restype = _i32
     L.lkl_backward_grouped.argtypes = [_i32, _G, _vp, _P, _vp, _vp, _sz, _vp]
+    L.lkl_backward_plan.restype = _i32
+    L.lkl_backward_plan.argtypes = [_P, _i32, _sz, _i32, ctypes.POINTER(ctypes.c_int32)]
     L.lkl_forward_noalloc.restype = _i32
     L.lkl_forward_noalloc.argtypes = [_vp, _vp, _vp, _vp, _vp, _P, _vp, _vp, _vp, _vp]
 

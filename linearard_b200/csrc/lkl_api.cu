@@ -541,6 +541,22 @@ int32_t lkl_backward_strided(const void* qs, const void* ks, const float* lse_s,
                        ws_bytes, stream);
 }
 
+int32_t lkl_backward_plan(const lkl_problem* p, int32_t has_mask, size_t ws_bytes, int32_t fused,
+                          int32_t* n_chunks) {
+  if (!n_chunks) return LKL_ERR_NULL_POINTER;
+  int32_t s = check_problem(p, true);
+  if (s) return s;
+  *n_chunks = 0;
+  const Problem q = to_problem(p);
+  if (p->B == 0 || p->T == 0 || lkl::sm100_dbuf_bytes(q) == 0) return LKL_OK;
+  const size_t base = lkl_workspace_size(p, has_mask);
+  if (ws_bytes < base + lkl::sm100_dbuf_min_bytes(q)) return LKL_ERR_WORKSPACE;
+  const int n = lkl::sm100_backward_chunks(q, ws_bytes - base, fused != 0);
+  if (n < 0) return LKL_ERR_WORKSPACE;
+  *n_chunks = n;
+  return LKL_OK;
+}
+
 int32_t lkl_device_status(void) {
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, lkl::g_device_error, sizeof(int)) != cudaSuccess)

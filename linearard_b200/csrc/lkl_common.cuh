@@ -118,6 +118,9 @@ bool sm100_backward_supports(const Problem& p);
 size_t sm100_dbuf_bytes(const Problem& p);
 // Smallest D buffer the backward runs with (one query-tile row of a kv group).
 size_t sm100_dbuf_min_bytes(const Problem& p);
+// Chunks (dq + dk launch pairs) of the backward with a D buffer of dbuf_bytes,
+// or -1 when it is too small (host-only).
+int sm100_backward_chunks(const Problem& p, size_t dbuf_bytes, bool alias);
 
 // Grouped calls (all items on the tensor-core path; `base` holds the shared
 // fields).  `desc` is sm100_group_desc_bytes(n) of device scratch for the

@@ -1390,6 +1390,13 @@ size_t sm100_dbuf_bytes(const Problem& p) {
   return (size_t)(std::max(std::min(all, cap), row) * kDTileBytes);
 }
 
+int sm100_backward_chunks(const Problem& p, size_t dbuf_bytes, bool alias) {
+  std::vector<Chunk> plan;
+  bool zero_dq = false;
+  if (!plan_chunks(p, (long long)(dbuf_bytes / kDTileBytes), alias, plan, zero_dq)) return -1;
+  return (int)plan.size();
+}
+
 size_t sm100_dbuf_min_bytes(const Problem& p) {
   if (sm100_dbuf_bytes(p) == 0) return 0;
   return (size_t)((long long)(p.Hq / p.Hkv_s) * ((p.T + kBM - 1) / kBM) * kDTileBytes);

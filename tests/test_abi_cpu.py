@@ -230,3 +230,36 @@ def test_grouped_entry_points_validate_before_device():
                                  None) == 2
     assert L.lkl_forward_grouped(1, one, None, ctypes.byref(shared), c(fake), c(fake), 16,
                                  None) == 6
+
+
+def _plan(p, ws=None, fused=1, mask=0):
+    L = _lib.lib()
+    if ws is None:
+        ws = L.lkl_backward_workspace_size(ctypes.byref(p), mask)
+    n = ctypes.c_int32(-1)
+    st = L.lkl_backward_plan(ctypes.byref(p), mask, ws, fused, ctypes.byref(n))
+    return st, n.value
+
+
+def test_backward_plan_chunks():
+    """The chunk planner of the tensor-core backward, host-only."""
+    L = _lib.lib()
+    # everything fits: one chunk
+    assert _plan(_prob(Hkv_t=2)) == (0, 1)
+    # LLaMA3-8B at 32K with the default workspace: Q/Q 32 heads -> 5 chunks, K/K 8 -> 2
+    qq = _prob(B=1, Hq=32, Hkv_s=32, Hkv_t=32, T=32768)
+    kk = _prob(B=1, Hq=8, Hkv_s=8, Hkv_t=8, T=32768)
+    assert _plan(qq) == (0, 5) and _plan(kk) == (0, 2)
+    # a workspace for two kv groups' tiles: ceil(4 groups / 2) chunks (Hq 4, Hkv 4)
+    p = _prob(Hq=4, Hkv_s=4, Hkv_t=4, T=1300)
+    n_t = (1300 + 127) // 128
+    base = L.lkl_workspace_size(ctypes.byref(p), 0)
+    per_head = n_t * (n_t + 1) // 2 * 32768
+    assert _plan(p, base + 2 * per_head) == (0, 2)
+    # less than one group: query-tile ranges of one group at a time (more chunks)
+    st, n = _plan(p, base + per_head // 3)
+    assert st == 0 and n > 4
+    # below one query-tile row of tiles: refused
+    assert _plan(p, base + (n_t - 1) * 32768)[0] == 6
+    # the CUDA-core shapes have no D buffer and no chunks
+    assert _plan(_prob(Ds=32, Dt=32)) == (0, 0)
