@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define LKL_ABI_VERSION 5
+#define LKL_ABI_VERSION 6
 
 /* element types of q/k tensors */
 enum lkl_dtype { LKL_F16 = 0, LKL_BF16 = 1 };
@@ -90,8 +90,16 @@ typedef struct lkl_problem {
 int32_t lkl_abi_version(void);
 const char* lkl_status_string(int32_t status);
 
-/* Bytes of scratch the entry points need for problem `p` (has_mask != 0 when a
- * padding mask will be passed).  Always a multiple of 256. */
+/* Bytes of scratch the forward entry points (lkl_lse, lkl_kl_forward,
+ * lkl_forward, lkl_forward_strided) need for problem `p` (has_mask != 0 when a
+ * padding mask will be passed): one fp32 partial per 32 query rows of each
+ * (batch, head) and, with a mask, the mask packed to one bit per token.
+ * Always a multiple of 256.  Added in ABI version 6. */
+size_t lkl_forward_workspace_size(const lkl_problem* p, int32_t has_mask);
+
+/* lkl_forward_workspace_size plus the backward's per-row scratch (8 bytes per
+ * (batch, head, row)): enough for every single-problem entry point except the
+ * backward's D tiles (lkl_backward_workspace_size).  A multiple of 256. */
 size_t lkl_workspace_size(const lkl_problem* p, int32_t has_mask);
 
 /* Bytes of scratch lkl_backward needs: lkl_workspace_size plus, for the
@@ -231,9 +239,11 @@ int32_t lkl_backward_grouped(int32_t n, const lkl_group_item* items, const void*
 int32_t lkl_backward_plan(const lkl_problem* p, int32_t has_mask, size_t workspace_bytes,
                           int32_t fused, int32_t* n_chunks);
 
-/* Device-side error word of the current device: the bounded waits inside the
+/* Device-side error word of the CURRENT device: the bounded waits inside the
  * tensor-core kernels set it instead of hanging.  Reads (synchronously) and
- * clears it; returns LKL_OK or LKL_ERR_DEVICE_TIMEOUT. */
+ * clears it; returns LKL_OK or LKL_ERR_DEVICE_TIMEOUT.  The word is per
+ * device: a process that drives several GPUs calls this once with each of
+ * them current (cudaSetDevice). */
 int32_t lkl_device_status(void);
 
 /* Which implementation the last lkl_forward / lkl_backward call on this host
@@ -262,8 +272,13 @@ void lkl_set_force_generic(int32_t force);
  * lkl_forward; the scratch comes from a fixed LKL_NOALLOC_SCRATCH_BYTES array
  * inside the library, which every GPU that loads the library keeps until the
  * process exits.
- *  - Limit: problems whose lkl_workspace_size() exceeds LKL_NOALLOC_SCRATCH_BYTES
- *    are refused with LKL_ERR_TOO_LARGE (use lkl_forward with a workspace).
+ *  - Limit: problems whose lkl_forward_workspace_size() exceeds
+ *    LKL_NOALLOC_SCRATCH_BYTES are refused with LKL_ERR_TOO_LARGE (use
+ *    lkl_forward with a workspace).  That size is 4 bytes per 32 query rows of
+ *    each (batch, head), rounded up to 256, plus with a mask 4 bytes per 32
+ *    tokens of each sequence, rounded up to 256: e.g. 8 sequences x 32 heads x
+ *    32K tokens without a mask (exactly 1 MiB), or one sequence of 32 heads x
+ *    248K tokens with a mask.
  *  - The first call on each device looks up the array's device address
  *    (cudaGetSymbolAddress, with that device current); make that first call
  *    before any stream capture.

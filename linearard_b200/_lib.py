@@ -32,7 +32,7 @@ EXPORTS = ("lkl_abi_version", "lkl_status_string", "lkl_workspace_size", "lkl_ls
            "lkl_last_path", "lkl_set_force_generic", "lkl_forward_noalloc",
            "lkl_last_cuda_error", "lkl_backward_workspace_size", "lkl_forward_strided",
            "lkl_backward_strided", "lkl_grouped_workspace_size", "lkl_forward_grouped",
-           "lkl_backward_grouped", "lkl_backward_plan")
+           "lkl_backward_grouped", "lkl_backward_plan", "lkl_forward_workspace_size")
 
 
 class LKLProblem(ctypes.Structure):
@@ -82,6 +82,8 @@ def _declare(L):
     L.lkl_status_string.argtypes = [_i32]
     L.lkl_workspace_size.restype = _sz
     L.lkl_workspace_size.argtypes = [_P, _i32]
+    L.lkl_forward_workspace_size.restype = _sz
+    L.lkl_forward_workspace_size.argtypes = [_P, _i32]
     L.lkl_backward_workspace_size.restype = _sz
     L.lkl_backward_workspace_size.argtypes = [_P, _i32]
     L.lkl_lse.restype = _i32

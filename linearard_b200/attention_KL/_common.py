@@ -88,7 +88,8 @@ def problem(qs, ks, qt=None, kt=None, causal=True, mask_dtype=_lib.LKL_MASK_U8,
 
 
 def workspace(prob: _lib.LKLProblem, has_mask: bool, device, backward: bool = False):
-    size_fn = _lib.lib().lkl_backward_workspace_size if backward else _lib.lib().lkl_workspace_size
+    L = _lib.lib()
+    size_fn = L.lkl_backward_workspace_size if backward else L.lkl_forward_workspace_size
     n = int(size_fn(ctypes.byref(prob), 1 if has_mask else 0))
     ws = torch.empty(max(n, 256), dtype=torch.uint8, device=device)
     return ws, n

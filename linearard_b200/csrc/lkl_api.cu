@@ -86,8 +86,9 @@ int32_t check_mask(const void* mask, int mdt) {
   return aligned(mask, es) ? LKL_OK : LKL_ERR_MISALIGNED;
 }
 
-int32_t check_workspace(const lkl_problem* p, const void* mask, void* ws, size_t ws_bytes) {
-  const size_t need = lkl_workspace_size(p, mask != nullptr);
+// `need` is lkl_forward_workspace_size for the forward entry points and
+// lkl_workspace_size (which adds the backward's per-row offsets) for lkl_backward.
+int32_t check_workspace(size_t need, void* ws, size_t ws_bytes) {
   if (need == 0) return LKL_OK;
   if (!ws || ws_bytes < need || !aligned(ws, 256)) return LKL_ERR_WORKSPACE;
   return LKL_OK;
@@ -176,13 +177,17 @@ const char* lkl_status_string(int32_t s) {
   }
 }
 
-size_t lkl_workspace_size(const lkl_problem* p, int32_t has_mask) {
+size_t lkl_forward_workspace_size(const lkl_problem* p, int32_t has_mask) {
   if (!p || p->B <= 0 || p->T <= 0 || p->Hq <= 0) return 0;
   const Problem q = to_problem(p);
   size_t n = round256((size_t)max_partials(q) * sizeof(float));
   if (has_mask) n += bits_bytes(p);
-  n += lsc_bytes(p);
   return n;
+}
+
+size_t lkl_workspace_size(const lkl_problem* p, int32_t has_mask) {
+  const size_t n = lkl_forward_workspace_size(p, has_mask);
+  return n == 0 ? 0 : n + lsc_bytes(p);
 }
 
 size_t lkl_backward_workspace_size(const lkl_problem* p, int32_t has_mask) {
@@ -199,7 +204,7 @@ int32_t lkl_lse(const void* q, const void* k, const void* mask, const lkl_proble
   if (!aligned(q, 2) || !aligned(k, 2) || !aligned(lse, 4)) return LKL_ERR_MISALIGNED;
   if ((s = check_mask(mask, p->mask_dtype))) return s;
   if (p->B == 0 || p->T == 0) return LKL_OK;
-  if ((s = check_workspace(p, mask, ws, ws_bytes))) return s;
+  if ((s = check_workspace(lkl_forward_workspace_size(p, mask != nullptr), ws, ws_bytes))) return s;
   if (!bind_device_of(q) || !device_is_sm100()) return LKL_ERR_NO_DEVICE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint32_t* bits;
@@ -226,7 +231,7 @@ int32_t lkl_kl_forward(const void* qs, const void* ks, const float* lse_s, const
   if ((s = check_mask(mask, p->mask_dtype))) return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (p->B == 0 || p->T == 0) return launch_status(cudaMemsetAsync(loss, 0, sizeof(float), st));
-  if ((s = check_workspace(p, mask, ws, ws_bytes))) return s;
+  if ((s = check_workspace(lkl_forward_workspace_size(p, mask != nullptr), ws, ws_bytes))) return s;
   if (!bind_device_of(qs) || !device_is_sm100()) return LKL_ERR_NO_DEVICE;
   uint32_t* bits;
   if ((s = prepare_mask(p, mask, ws, &bits, st))) return s;
@@ -275,7 +280,7 @@ int32_t forward_impl(const void* qs, const void* ks, const void* qt, const void*
   if (strides && (s = check_strides(strides, ptrs))) return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (p->B == 0 || p->T == 0) return launch_status(cudaMemsetAsync(loss, 0, sizeof(float), st));
-  if ((s = check_workspace(p, mask, ws, ws_bytes))) return s;
+  if ((s = check_workspace(lkl_forward_workspace_size(p, mask != nullptr), ws, ws_bytes))) return s;
   if (!bind_device_of(qs) || !device_is_sm100()) return LKL_ERR_NO_DEVICE;
   const Problem q = to_problem(p);
   const bool tc = use_tensor_cores(q, qs, ks, qt, kt);
@@ -320,14 +325,19 @@ int32_t backward_impl(const void* qs, const void* ks, const float* lse_s, const 
                            strides[0].t != strides[1].t))
     return LKL_ERR_BAD_ALIAS;
   if (p->B == 0 || p->T == 0) return LKL_OK;
-  if ((s = check_workspace(p, mask, ws, ws_bytes))) return s;
-  // the tensor-core backward needs room for at least one chunk of D tiles
-  // beyond the common scratch; more room means fewer, larger chunks
   const size_t base = lkl_workspace_size(p, mask != nullptr);
-  if (ws_bytes < base + lkl::sm100_dbuf_min_bytes(to_problem(p))) return LKL_ERR_WORKSPACE;
-  if (!bind_device_of(qs) || !device_is_sm100()) return LKL_ERR_NO_DEVICE;
+  if ((s = check_workspace(base, ws, ws_bytes))) return s;
   const Problem q = to_problem(p);
-  const bool tc = use_tensor_cores(q, qs, ks, qt, kt) && lkl::sm100_backward_supports(q);
+  // the tensor-core backward needs room for at least one chunk of D tiles
+  // beyond the common scratch (more room means fewer, larger chunks); the
+  // CUDA-core backward needs none.  Decided from shape, alignment and the
+  // force flag alone, so it is checked before any device work.
+  const bool tc_shape = !g_force_generic.load() && aligned(qs, 16) && aligned(ks, 16) &&
+                        aligned(qt, 16) && aligned(kt, 16) && lkl::sm100_shape_ok(q);
+  if (tc_shape && ws_bytes < base + lkl::sm100_dbuf_min_bytes(q)) return LKL_ERR_WORKSPACE;
+  if (!bind_device_of(qs) || !device_is_sm100()) return LKL_ERR_NO_DEVICE;
+  const bool tc = tc_shape && use_tensor_cores(q, qs, ks, qt, kt) &&
+                  lkl::sm100_backward_supports(q);
   if (strides && !tc) return LKL_ERR_UNSUPPORTED;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint32_t* bits;

@@ -22,10 +22,12 @@
 
 namespace {
 
-// LKL_NOALLOC_SCRATCH_BYTES (1 MiB): per-tile partials (4 B per 32 query rows
-// of each batch x head) plus the packed mask (4 B per 32 tokens of each
-// sequence) -- enough for, e.g., 32 heads x 256K tokens, or 8 sequences x 32
-// heads x 32K tokens.
+// LKL_NOALLOC_SCRATCH_BYTES (1 MiB) holds what the forward needs
+// (lkl_forward_workspace_size): per-tile partials (4 B per 32 query rows of
+// each batch x head, rounded up to 256 B) plus, with a mask, the packed mask
+// (4 B per 32 tokens of each sequence, rounded up to 256 B).  That is enough
+// for 8 sequences x 32 heads x 32K tokens without a mask (exactly 1 MiB), or
+// one sequence of 32 heads x 248K tokens with a mask.
 constexpr size_t kNoAllocScratchBytes = LKL_NOALLOC_SCRATCH_BYTES;
 constexpr int kMaxDevices = 64;
 
@@ -65,7 +67,7 @@ int32_t lkl_forward_noalloc(const void* qs, const void* ks, const void* qt, cons
                             float* loss, void* stream) {
   if (!p) return LKL_ERR_NULL_POINTER;
   // Size limit first, so an oversized problem is refused before any CUDA call.
-  const size_t need = lkl_workspace_size(p, mask != nullptr);
+  const size_t need = lkl_forward_workspace_size(p, mask != nullptr);
   if (need > kNoAllocScratchBytes) return LKL_ERR_TOO_LARGE;
   int32_t status = LKL_OK;
   void* scratch = nullptr;

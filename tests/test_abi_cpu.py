@@ -55,6 +55,15 @@ def test_workspace_size():
     assert n0 >= 4 * 1 * 4 * ((300 + 31) // 32)
     assert n1 - n0 >= 1 * ((300 + 31) // 32) * 4
     assert L.lkl_workspace_size(ctypes.byref(_prob(T=0)), 1) == 0
+    # the forward entry points need only the partials and the mask bits; the
+    # common size adds the backward's 8 bytes per (batch, head, row)
+    f0 = L.lkl_forward_workspace_size(ctypes.byref(p), 0)
+    f1 = L.lkl_forward_workspace_size(ctypes.byref(p), 1)
+    assert f0 == 256 * ((4 * 4 * ((300 + 31) // 32) + 255) // 256)
+    assert f1 == f0 + 256
+    assert n0 == f0 + 256 * ((8 * 4 * 300 + 255) // 256)
+    assert n1 == f1 + (n0 - f0)
+    assert L.lkl_forward_workspace_size(ctypes.byref(_prob(T=0)), 1) == 0
 
 
 def test_backward_workspace_holds_the_d_tiles():
