@@ -246,6 +246,16 @@ int32_t lkl_backward_plan(const lkl_problem* p, int32_t has_mask, size_t workspa
  * them current (cudaSetDevice). */
 int32_t lkl_device_status(void);
 
+/* Diagnostic (ABI version 6; no counterpart in the reference): launches, on
+ * `stream` of the current device, one CTA whose mbarrier wait can never
+ * complete, using the same bounded wait as the tensor-core kernels but with a
+ * limit of `limit_us` microseconds (1 .. 2,000,000; LKL_ERR_BAD_SHAPE
+ * otherwise).  The wait gives up, sets the device error word and the kernel
+ * returns, so after the stream is synchronised lkl_device_status() reports
+ * LKL_ERR_DEVICE_TIMEOUT (and clears it) and the context stays usable.  For
+ * tests of the failure path; it touches no other state. */
+int32_t lkl_selftest_bounded_wait(uint32_t limit_us, void* stream);
+
 /* Which implementation the last lkl_forward / lkl_backward call on this host
  * thread dispatched to: 1 = sm_100a tensor-core kernels, 0 = generic CUDA-core
  * kernels (head dims or alignments the tensor-core kernels do not cover). */

@@ -32,7 +32,8 @@ EXPORTS = ("lkl_abi_version", "lkl_status_string", "lkl_workspace_size", "lkl_ls
            "lkl_last_path", "lkl_set_force_generic", "lkl_forward_noalloc",
            "lkl_last_cuda_error", "lkl_backward_workspace_size", "lkl_forward_strided",
            "lkl_backward_strided", "lkl_grouped_workspace_size", "lkl_forward_grouped",
-           "lkl_backward_grouped", "lkl_backward_plan", "lkl_forward_workspace_size")
+           "lkl_backward_grouped", "lkl_backward_plan", "lkl_forward_workspace_size",
+           "lkl_selftest_bounded_wait")
 
 
 class LKLProblem(ctypes.Structure):
@@ -95,6 +96,8 @@ def _declare(L):
     L.lkl_backward.restype = _i32
     L.lkl_backward.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _P, _vp, _vp, _vp, _vp, _sz, _vp]
     L.lkl_device_status.restype = _i32
+    L.lkl_selftest_bounded_wait.restype = _i32
+    L.lkl_selftest_bounded_wait.argtypes = [ctypes.c_uint32, _vp]
     L.lkl_last_path.restype = _i32
     L.lkl_last_cuda_error.restype = _i32
     L.lkl_set_force_generic.restype = None

@@ -579,6 +579,14 @@ int32_t lkl_device_status(void) {
   return LKL_OK;
 }
 
+int32_t lkl_selftest_bounded_wait(uint32_t limit_us, void* stream) {
+  if (limit_us == 0 || limit_us > 2000000u) return LKL_ERR_BAD_SHAPE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || !device_is_sm100()) return LKL_ERR_NO_DEVICE;
+  return launch_status(lkl::launch_bounded_wait_probe((uint64_t)limit_us * 1000u,
+                                                      static_cast<cudaStream_t>(stream)));
+}
+
 int32_t lkl_last_path(void) { return t_last_path; }
 
 int32_t lkl_last_cuda_error(void) { return t_last_cuda_error; }

@@ -143,4 +143,7 @@ cudaError_t launch_sm100_backward(const Problem& p, const void* qs, const void* 
                                   bool alias, float2* lsc, void* dbuf, size_t dbuf_bytes,
                                   cudaStream_t st);
 
+// Diagnostic launch of a bounded wait that cannot complete (limit in ns).
+cudaError_t launch_bounded_wait_probe(uint64_t limit_ns, cudaStream_t st);
+
 }  // namespace lkl

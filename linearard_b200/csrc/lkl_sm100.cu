@@ -1519,4 +1519,28 @@ cudaError_t launch_sm100_backward_grouped(const Problem& base, const GroupSpec* 
                        static_cast<uint16_t*>(dbuf), ref, st);
 }
 
+// Diagnostic: one CTA whose mbarrier never completes (nothing arrives on it).
+// Two waiters in different warps run the kernels' own bounded wait with a
+// short limit: the first to run out sets the CTA abort flag and the device
+// error word, the other sees the flag, and the kernel returns -- the path a
+// stalled pipeline takes instead of hanging the GPU.
+__global__ void __launch_bounds__(64, 1) bounded_wait_probe_kernel(uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0)
+    mbar_wait_for(&bar, 0, &abort_flag, &g_device_error, limit_ns);
+  __syncthreads();
+}
+
+cudaError_t launch_bounded_wait_probe(uint64_t limit_ns, cudaStream_t st) {
+  bounded_wait_probe_kernel<<<1, 64, 0, st>>>(limit_ns);
+  return cudaGetLastError();
+}
+
 }  // namespace lkl

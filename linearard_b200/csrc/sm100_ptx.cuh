@@ -57,21 +57,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // so a broken pipeline ends the kernel instead of hanging the GPU.
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s; one tile takes microseconds
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          int* err_word) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                              int* err_word, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > kTimeoutNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         *abort = 1;
         atomicExch(err_word, 1);
         return false;
       }
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          int* err_word) {
+  return mbar_wait_for(bar, parity, abort, err_word, kTimeoutNs);
 }
 
 // ------------------------------------------------------------------ TMA

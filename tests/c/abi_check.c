@@ -32,6 +32,9 @@ int main(void) {
   const size_t n_t = (300 + 127) / 128;
   CHECK(fwd > 0 && fwd % 256 == 0);
   CHECK(bwd == fwd + 4 * (n_t * (n_t + 1) / 2) * 32768);  /* one 32 KB D tile per pair */
+  /* the forward entry points need less: no per-row backward offsets */
+  CHECK(lkl_forward_workspace_size(&p, 0) + 256 * ((8 * 4 * 300 + 255) / 256) == fwd);
+  CHECK(lkl_selftest_bounded_wait(0, NULL) == LKL_ERR_BAD_SHAPE);
 
   void* fake = (void*)(uintptr_t)0x10000;
   float* ff = (float*)fake;

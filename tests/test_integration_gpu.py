@@ -98,47 +98,6 @@ def test_identical_student_teacher_gives_zero():
     assert float(s.grad.abs().max()) < 1e-3
 
 
-def test_tensor_core_matches_generic_at_8k():
-    """LLaMA2-7B config shape (n=8192, d=128) on a few heads: the tensor-core
-    kernels and the generic kernels agree (size-independent cross-check), and
-    every row KL is non-negative in sum."""
-    from linearard_b200.attention_KL import attn_kl_forward, kl_backward
-    from linearard_b200.synth import relation_pair
-    s, t = relation_pair((1, 4, 8192, 128), seed_teacher=0, seed_student=1, theta=1e4,
-                         apply_rope=True, channel_scale=True, device="cuda")
-    loss, ls, lt = attn_kl_forward(s, s, t, t)
-    assert path_is_tensor_core()
-    dS, _ = kl_backward(s, s, ls, t, t, lt, fused=True)
-    with force_generic():
-        loss_g, ls_g, lt_g = attn_kl_forward(s, s, t, t)
-        dS_g, _ = kl_backward(s, s, ls_g, t, t, lt_g, fused=True)
-    torch.cuda.synchronize()
-    check_device_status()
-    assert float(loss) > 0
-    assert_loss_close(float(loss), float(loss_g))
-    torch.testing.assert_close(ls, ls_g, rtol=1e-4, atol=1e-3)
-    assert_grad_close(dS.cpu().numpy(), dS_g.cpu().numpy(), "dS")
-
-
-@pytest.mark.slow
-def test_llama3_32k_one_head_vs_oracle_slice():
-    """Config-3 generator at n=32768: the first 2048 rows of a causal loss depend
-    only on the first 2048 tokens, so a 2048-token prefix run through the
-    numpy oracle pins the full-length kernel's row LSEs there."""
-    from linearard_b200.attention_KL import attn_kl_forward
-    from linearard_b200.synth import relation_pair
-    s, t = relation_pair((1, 1, 32768, 128), seed_teacher=0, seed_student=1, theta=5e5,
-                         apply_rope=True, device="cuda")
-    loss, ls, lt = attn_kl_forward(s, s, t, t)
-    torch.cuda.synchronize()
-    n = 2048
-    a, b = C.to_np(s[:, :, :n].cpu()), C.to_np(t[:, :, :n].cpu())
-    _, rls, rlt = O.oracle_attn_kl_align(a, a, b, b)
-    np.testing.assert_allclose(ls[:, :, :n].cpu().numpy(), rls, rtol=1e-4, atol=1e-4)
-    np.testing.assert_allclose(lt[:, :, :n].cpu().numpy(), rlt, rtol=1e-4, atol=1e-4)
-    assert np.isfinite(float(loss)) and float(loss) > 0
-
-
 def test_backward_from_a_fresh_host_thread():
     """PyTorch runs backward on its own worker thread, which may have no
     current CUDA context; every entry point binds the device of its inputs
