@@ -11,6 +11,10 @@ one sequence per GPU).
 Prints ONE JSON line on rank 0.  ``--impl reference`` times LinearARD's
 materialised CPU formulation (the numpy restatement in ``oracle/``) on the
 host cores on a bounded sample and extrapolates it to the same workload.
+``--impl reference-gpu`` times LinearARD's own Triton kernels (an unmodified
+copy of ``kernels/attention_KL`` under ``baseline/_ref/``, not part of this
+repository) on the same GPU workload through their ``attn_kl_align``, as a
+context number; it prints an ``unavailable`` line when that copy is absent.
 """
 from __future__ import annotations
 
@@ -37,7 +41,7 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-gpu"])
     ap.add_argument("--config", default=WORKLOAD)
     ap.add_argument("--cpu-sample-n", type=int, default=2048)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -100,6 +104,20 @@ def cpu_sample(cfg, n: int, min_seconds: float = 10.0):
                                 f"median of {len(times)} runs = {per_relhead:.3f} s; extrapolated "
                                 f"x(n_full/n)^2 x {cfg.rel_heads} rel-heads",
                       "per_relhead_s": per_relhead}
+
+
+def cpu_baseline_fit(cfg, n_small: int = 2048, n_large: int = 4096):
+    """The CPU baseline at two lengths: the cost exponent fitted between them
+    (the n^2 extrapolation assumes 2) and the extrapolation from the larger."""
+    import math
+    v_s, info_s = cpu_sample(cfg, n_small, min_seconds=6.0)
+    v_l, info_l = cpu_sample(cfg, n_large, min_seconds=0.0)
+    expo = math.log(info_l["per_relhead_s"] / info_s["per_relhead_s"]) / math.log(n_large / n_small)
+    info_l["sample"] += (f"; also n={n_small}: {info_s['per_relhead_s']:.3f} s per rel-head "
+                         f"(fitted cost exponent {expo:.2f} between n={n_small} and {n_large})")
+    info_l["exponent_fit"] = expo
+    info_l["per_n_tokens_s"] = {str(n_small): v_s, str(n_large): v_l}
+    return v_l, info_l
 
 
 def use_all_cpu_threads():
@@ -165,6 +183,85 @@ def config_block(cfg, n):
         "parallelism": f"dp{n} (one sequence per GPU, scalar loss all-reduced)"}
 
 
+# ------------------------------------------------------------------ reference Triton kernels
+def run_reference_gpu(args):
+    """--impl reference-gpu: LinearARD's Triton attn_kl_align (integration.py:70-73
+    -> kernel_A.py:190, kernel_B.py:249, kernel_C.py:293), unmodified, from
+    baseline/_ref, on the same synthetic relations, timed like our arm."""
+    ref_root = os.path.join(ROOT, "baseline", "_ref")
+    rank = int(os.environ.get("RANK", "0"))
+    if not os.path.exists(os.path.join(ref_root, "kernels", "attention_KL", "integration.py")):
+        if rank == 0:
+            print(json.dumps({"impl": "reference-gpu", "unavailable":
+                              "no copy of LinearARD's kernels/attention_KL under baseline/_ref"}))
+        return
+    import torch
+    sys.path.insert(0, ref_root)
+    from kernels.attention_KL.integration import attn_kl_align as ref_align
+
+    from linearard_b200.synth import CONFIGS, make_relations
+    if rank != 0:
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = CONFIGS[args.config]
+    rels = make_relations(cfg, device=dev, seed=0)
+    students = {r: st.requires_grad_(True) for r, (st, _) in rels.items()}
+
+    def step():
+        total = None
+        for r in cfg.relations:
+            l = ref_align(students[r], students[r], rels[r][1], rels[r][1], None, cfg.causal)
+            total = l if total is None else total + l
+        total.backward()
+        for t in students.values():
+            t.grad = None
+        return total.detach()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    with ClockSampler(0) as clk:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for _ in range(args.steps):
+            loss = step()
+        ev1.record()
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    value = cfg.seq_len * cfg.batch / (ms / 1e3)
+    print(json.dumps({
+        "impl": "reference-gpu", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": config_block(cfg, 1), "step_tflops": cfg.algorithmic_flops() / (ms / 1e3) / 1e12,
+        "clocks": clk.summary(), "loss": float(loss),
+        "what": "LinearARD's Triton kernels (unmodified copy under baseline/_ref), same step"}),
+        flush=True)
+
+
+def gpu_local_cpus(dev):
+    """CPUs of the NUMA node that the GPU's PCIe device reports (sysfs
+    local_cpulist), or None when that cannot be read."""
+    try:
+        import torch
+        pr = torch.cuda.get_device_properties(dev)
+        bus = "%04x:%02x:%02x.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+        with open(f"/sys/bus/pci/devices/{bus}/local_cpulist") as f:
+            spec = f.read().strip()
+        cpus = set()
+        for part in spec.split(","):
+            if "-" in part:
+                a, b = part.split("-")
+                cpus.update(range(int(a), int(b) + 1))
+            elif part:
+                cpus.add(int(part))
+        cpus &= os.sched_getaffinity(0)
+        return cpus or None
+    except Exception:  # noqa: BLE001 -- no sysfs entry / no PCI info: leave placement alone
+        return None
+
+
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -226,6 +323,9 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.impl == "reference-gpu":
+        run_reference_gpu(args)
         return
 
     import torch
@@ -343,6 +443,14 @@ def main():
         # (the loss is a sum over heads).  All copies go out on a copy stream at
         # the start of the step; the forward of slice k waits only for slice k's
         # copy, so the PCIe transfer of later slices runs under earlier compute.
+        numa = gpu_local_cpus(dev)
+        saved_affinity = None
+        if numa:
+            # pinned staging pages are placed on the NUMA node of this GPU's
+            # PCIe root (first touch by a thread running there), so the copy
+            # engines of N GPUs do not all read across the socket link
+            saved_affinity = os.sched_getaffinity(0)
+            os.sched_setaffinity(0, numa)
         slices = []
         for ri, r in enumerate(cfg.relations):
             H = students[r].shape[1]
@@ -357,6 +465,8 @@ def main():
                 ht = teachers[r][:, h0:h1].contiguous().cpu().pin_memory()
                 slices.append((hs, ht, torch.empty_like(hs, device=dev),
                                torch.empty_like(ht, device=dev)))
+        if saved_affinity is not None:
+            os.sched_setaffinity(0, saved_affinity)
         h2d = sum(x.numel() * x.element_size() for sl in slices for x in sl[:2])
         copy_stream = torch.cuda.Stream(device=dev)
         copied = [torch.cuda.Event() for _ in slices]
@@ -394,16 +504,39 @@ def main():
         e_ms = torch.tensor([k0.elapsed_time(k1)], device=dev)
         if world > 1:
             dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        # the host path alone: the same copies, every rank at once, no compute
+        # (the ceiling the overlapped step can approach)
+        barrier()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(copy_stream)
+        with torch.cuda.stream(copy_stream):
+            for _ in range(args.steps):
+                for hs, ht, ds, dt in slices:
+                    ds.copy_(hs, non_blocking=True)
+                    dt.copy_(ht, non_blocking=True)
+        c1.record(copy_stream)
+        barrier()
+        c_ms = torch.tensor([c0.elapsed_time(c1) / args.steps], device=dev)
+        if world > 1:
+            dist.all_reduce(c_ms, op=dist.ReduceOp.MAX)
+        e_step = float(e_ms.item()) / args.steps
+        copy_ms = float(c_ms.item())
         e2e = {"value": tokens / (float(e_ms.item()) / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4,
-               "ms_per_step": float(e_ms.item()) / args.steps}
+               "ms_per_step": e_step,
+               "h2d_copy_only_ms_per_step": copy_ms,
+               "h2d_gbs_per_rank_copy_only": h2d / (copy_ms / 1e3) / 1e9,
+               "exposed_ms_per_step": e_step - ms_step,
+               "bound": "host->device copies" if copy_ms >= ms_step else "device compute",
+               "staging_numa_local": bool(numa)}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         use_all_cpu_threads()
-        v, info = cpu_sample(cfg, args.cpu_sample_n, min_seconds=10.0)
+        v, info = cpu_baseline_fit(cfg)
         cpu = {"value": v, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
-               "sample": info["sample"]}
+               "sample": info["sample"], "exponent_fit": info["exponent_fit"],
+               "tokens_s_by_sample_n": info["per_n_tokens_s"]}
 
     if rank == 0:
         out = {
