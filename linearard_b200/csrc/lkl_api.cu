@@ -213,7 +213,14 @@ int32_t lkl_lse(const void* q, const void* k, const void* mask, const lkl_proble
   pp.Hkv_t = p->Hkv_s;
   pp.Dt = p->Ds;
   pp.dtype_t = p->dtype_s;
+  pp.sm_scale_t = p->sm_scale_s;
   const Problem qq = to_problem(&pp);
+  if (use_tensor_cores(qq, q, k, q, k)) {
+    t_last_path = 1;
+    return launch_status(lkl::launch_sm100_forward(qq, q, k, q, k, nullptr, bits, lse, nullptr,
+                                                   nullptr, nullptr, st, 0));
+  }
+  t_last_path = 0;
   return launch_status(lkl::launch_generic_forward(0, qq, q, k, q, k, bits, lse, nullptr,
                                                    nullptr, nullptr, st));
 }
@@ -238,9 +245,16 @@ int32_t lkl_kl_forward(const void* qs, const void* ks, const float* lse_s, const
   const Problem q = to_problem(p);
   float* part = partials_ptr(p, mask, ws);
   int np = 0;
-  cudaError_t e = lkl::launch_generic_forward(2, q, qs, ks, qt, kt, bits,
-                                              const_cast<float*>(lse_s),
-                                              const_cast<float*>(lse_t), part, &np, st);
+  cudaError_t e;
+  if (use_tensor_cores(q, qs, ks, qt, kt)) {
+    t_last_path = 1;
+    e = lkl::launch_sm100_forward(q, qs, ks, qt, kt, nullptr, bits, const_cast<float*>(lse_s),
+                                  const_cast<float*>(lse_t), part, &np, st, 2);
+  } else {
+    t_last_path = 0;
+    e = lkl::launch_generic_forward(2, q, qs, ks, qt, kt, bits, const_cast<float*>(lse_s),
+                                    const_cast<float*>(lse_t), part, &np, st);
+  }
   if (e != cudaSuccess) return launch_status(e);
   return launch_status(lkl::launch_reduce_partials(part, np, loss, st));
 }

@@ -105,10 +105,14 @@ struct TensorStrides {
 };
 
 // `strides`: qs, ks, qt, kt strides, or nullptr for contiguous inputs.
+// mode 1: fused forward (lse_s, lse_t and KL partials); mode 0: lse_s of the
+// student pair only (the teacher fields of `p` must repeat the student's);
+// mode 2: KL partials from the given lse_s / lse_t.
 cudaError_t launch_sm100_forward(const Problem& p, const void* qs, const void* ks,
                                  const void* qt, const void* kt, const TensorStrides* strides,
                                  const uint32_t* bits, float* lse_s, float* lse_t,
-                                 float* partials, int* num_partials, cudaStream_t st);
+                                 float* partials, int* num_partials, cudaStream_t st,
+                                 int mode = 1);
 // Backward: per chunk, a dq launch that also stores the rounded D tiles into
 // `dbuf`, then a dk GEMM launch over them; no reductions.  `lsc` is B*Hq*T
 // float2 of scratch, `dbuf` at least

@@ -236,7 +236,167 @@ __device__ __forceinline__ void setup_cta(Misc* misc, int warp, int lane) {
 }
 
 // ============================================================== forward
-template <int DS, int DT>
+// Row warps of the LSE-only forward (MODE 0): online (max, sum) of the
+// student scores, merged across the four warpgroups; rows removed by the mask
+// get 0, rows with no valid column -inf (kernel_A.py:146-158).
+template <typename L>
+__device__ __forceinline__ void forward_rows_lse(Misc* misc, float* stat, const Problem& p,
+                                                 const Tile& t, const uint32_t* bits,
+                                                 float* lse_s, uint32_t tmem, int warp, int lane,
+                                                 volatile int* abort, int* err) {
+  const int wg = warp >> 2, q = warp & 3;
+  const int r = q * 32 + lane;
+  const int i = t.mt * kBM + r;
+  const int words = (p.T + 31) >> 5;
+  const bool row_in = i < p.T;
+  const bool row_valid = row_in && token_valid(bits, words, t.b, i);
+  const int lim = p.causal ? min(i, p.T - 1) : p.T - 1;
+  const float cs = p.sc_s * kLog2e;
+  float m_s = -CUDART_INF_F, l_s = 0.f;
+  const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+  const uint64_t cs2 = f2pack(cs, cs);
+  for (int j = 0; j < t.n_ct; ++j) {
+    const int bf = j & 1;
+    if (!mbar_wait(&misc->s_full[bf], (j >> 1) & 1, abort, err)) break;
+    tc_fence_after();
+    float x[32];
+    tmem_ld32(lane_addr + bf * 256 + wg * 32, x);
+    tmem_wait_ld_dep(x);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&misc->s_empty[bf]);
+    if (!row_valid) continue;
+    const int c0 = j * kBN + wg * 32;
+    if (!((c0 + 31 <= lim) && (bits == nullptr))) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k)
+        if (!((c0 + k <= lim) && token_valid(bits, words, t.b, c0 + k))) x[k] = -1.0e30f;
+    }
+    float mx = x[0];
+#pragma unroll
+    for (int k = 1; k < 31; k += 2) mx = fmax3(mx, x[k], x[k + 1]);
+    mx = fmaxf(mx, x[31]);
+    if (mx < -1.0e29f) continue;
+    const float ms_new = fmaxf(m_s, mx * cs);
+    l_s *= ex2(m_s - ms_new);
+    const uint64_t nms2 = f2pack(-ms_new, -ms_new);
+    uint64_t ls2 = 0;
+#pragma unroll
+    for (int k = 0; k < 32; k += 2) {
+      float a0, a1;
+      f2unpack(ffma2(f2pack(x[k], x[k + 1]), cs2, nms2), a0, a1);
+      ls2 = fadd2(ls2, f2pack(ex2(a0), ex2(a1)));
+    }
+    float s0, s1;
+    f2unpack(ls2, s0, s1);
+    l_s += s0 + s1;
+    m_s = ms_new;
+  }
+  if (wg > 0) {
+    stat[(wg - 1) * 2 * kBM + r] = m_s;
+    stat[((wg - 1) * 2 + 1) * kBM + r] = l_s;
+  }
+  named_bar(1, 32 * kRowWarps);
+  if (wg == 0 && row_in) {
+    float M = m_s;
+#pragma unroll
+    for (int g = 0; g < 3; ++g) M = fmaxf(M, stat[g * 2 * kBM + r]);
+    float Ls = 0.f;
+    if (M != -CUDART_INF_F) {
+      Ls = l_s * ex2(m_s - M);
+#pragma unroll
+      for (int g = 0; g < 3; ++g) Ls += stat[(g * 2 + 1) * kBM + r] * ex2(stat[g * 2 * kBM + r] - M);
+    }
+    const float v = (Ls > 0.f) ? (M + lg2(Ls)) * kLn2 : -CUDART_INF_F;
+    lse_s[(size_t)t.bh * p.T + i] = row_valid ? v : 0.f;
+  }
+}
+
+// Row warps of the KL forward given both LSEs (MODE 2): sum over valid j of
+// pt (log pt - log ps) with log p = s - lse, as kernel_B.py:57-218; rows that
+// the mask removes or whose LSE is -inf give 0.  Base-2 exponents
+// b = st log2e - lse_t log2e, a = ss log2e - lse_s log2e: the term is
+// 2^b (b - a) ln 2.
+template <typename L>
+__device__ __forceinline__ void forward_rows_kl_given_lse(
+    Misc* misc, float* stat, const Problem& p, const Tile& t, const uint32_t* bits,
+    const float* lse_s, const float* lse_t, float* partials, uint32_t tmem, int warp, int lane,
+    volatile int* abort, int* err) {
+  const int wg = warp >> 2, q = warp & 3;
+  const int r = q * 32 + lane;
+  const int i = t.mt * kBM + r;
+  const int words = (p.T + 31) >> 5;
+  const bool row_in = i < p.T;
+  bool row_ok = row_in && token_valid(bits, words, t.b, i);
+  float Ls = 0.f, Lt = 0.f;
+  if (row_in) {
+    Ls = lse_s[(size_t)t.bh * p.T + i];
+    Lt = lse_t[(size_t)t.bh * p.T + i];
+  }
+  row_ok = row_ok && Ls != -CUDART_INF_F && Lt != -CUDART_INF_F;
+  const int lim = p.causal ? min(i, p.T - 1) : p.T - 1;
+  const float cs = p.sc_s * kLog2e, ct = p.sc_t * kLog2e;
+  const uint64_t cs2 = f2pack(cs, cs), ct2 = f2pack(ct, ct);
+  const uint64_t nls2 = f2pack(-Ls * kLog2e, -Ls * kLog2e);
+  const uint64_t nlt2 = f2pack(-Lt * kLog2e, -Lt * kLog2e);
+  const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+  float acc = 0.f;
+  for (int j = 0; j < t.n_ct; ++j) {
+    const int bf = j & 1;
+    if (!mbar_wait(&misc->s_full[bf], (j >> 1) & 1, abort, err)) break;
+    tc_fence_after();
+    float x[32], y[32];
+    const uint32_t col = bf * 256 + wg * 32;
+    tmem_ld32(lane_addr + col, x);
+    tmem_ld32(lane_addr + col + 128, y);
+    tmem_wait_ld_dep(x);
+    tmem_wait_ld_dep(y);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&misc->s_empty[bf]);
+    if (!row_ok) continue;
+    const int c0 = j * kBN + wg * 32;
+    const bool full = (c0 + 31 <= lim) && (bits == nullptr);
+    uint64_t acc2 = 0;
+#pragma unroll
+    for (int k = 0; k < 32; k += 2) {
+      const uint64_t aa = ffma2(f2pack(x[k], x[k + 1]), cs2, nls2);
+      const uint64_t bb = ffma2(f2pack(y[k], y[k + 1]), ct2, nlt2);
+      float b0, b1;
+      f2unpack(bb, b0, b1);
+      float pt0 = ex2(b0), pt1 = ex2(b1);
+      if (!full) {
+        if (!((c0 + k <= lim) && token_valid(bits, words, t.b, c0 + k))) pt0 = 0.f;
+        if (!((c0 + k + 1 <= lim) && token_valid(bits, words, t.b, c0 + k + 1))) pt1 = 0.f;
+      }
+      acc2 = ffma2(f2pack(pt0, pt1), fsub2(bb, aa), acc2);
+    }
+    float a0, a1;
+    f2unpack(acc2, a0, a1);
+    acc += a0 + a1;
+  }
+  if (wg > 0) stat[(wg - 1) * kBM + r] = acc;
+  named_bar(1, 32 * kRowWarps);
+  if (wg == 0) {
+    float kl = acc;
+#pragma unroll
+    for (int g = 0; g < 3; ++g) kl += stat[g * kBM + r];
+    kl = row_ok ? kl * kLn2 : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) kl += __shfl_xor_sync(0xffffffffu, kl, o);
+    if (lane == 0) misc->red[q] = kl;
+    named_bar(2, 128);
+    if (q == 0 && lane == 0)
+      partials[blockIdx.x] = (misc->red[0] + misc->red[1]) + (misc->red[2] + misc->red[3]);
+  }
+}
+
+// MODE 1: the fused forward (both LSEs and the KL partials).  MODE 0: the
+// LSE of the student pair only (lkl_lse, kernel_A.py:42-159): one score GEMM
+// and one exponential per element.  MODE 2: the KL partials given both LSEs
+// (lkl_kl_forward, kernel_B.py:57-218): two score GEMMs, one exponential per
+// element and no running maxima.
+template <int DS, int DT, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
 sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs0,
                      const __grid_constant__ CUtensorMap tm_ks0,
@@ -246,6 +406,7 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs0,
                      float* __restrict__ lse_t0, float* __restrict__ partials,
                      const GroupRef gref) {
   using L = FwdLayout<DS, DT>;
+  constexpr bool kTeacher = MODE != 0;   // the teacher pair takes part
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   Misc* misc = reinterpret_cast<Misc*>(smem + L::OFF_MISC);
@@ -277,16 +438,18 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs0,
   if (warp == kProducerWarp) {
     if (lane == 0) {
       // ---------------- TMA producer
-      mbar_arrive_expect_tx(&misc->q_full, L::QS + L::QT);
+      mbar_arrive_expect_tx(&misc->q_full, L::QS + (kTeacher ? L::QT : 0));
       issue_tile_loads(smem + L::OFF_QS, &tm_qs, &misc->q_full, DS, t.mt * kBM, t.h, t.b);
-      issue_tile_loads(smem + L::OFF_QT, &tm_qt, &misc->q_full, DT, t.mt * kBM, t.h, t.b);
+      if (kTeacher)
+        issue_tile_loads(smem + L::OFF_QT, &tm_qt, &misc->q_full, DT, t.mt * kBM, t.h, t.b);
       for (int j = 0; j < t.n_ct; ++j) {
         const int s = j % L::NS;
         if (j >= L::NS && !mbar_wait(&misc->k_empty[s], ((j / L::NS) - 1) & 1, abort, err)) break;
         uint8_t* st = smem + L::OFF_K + s * L::STAGE;
-        mbar_arrive_expect_tx(&misc->k_full[s], L::STAGE);
+        mbar_arrive_expect_tx(&misc->k_full[s], kBN * DS * 2 + (kTeacher ? kBN * DT * 2 : 0));
         issue_tile_loads(st, &tm_ks, &misc->k_full[s], DS, j * kBN, t.hs, t.b);
-        issue_tile_loads(st + kBN * DS * 2, &tm_kt, &misc->k_full[s], DT, j * kBN, t.ht, t.b);
+        if (kTeacher)
+          issue_tile_loads(st + kBN * DS * 2, &tm_kt, &misc->k_full[s], DT, j * kBN, t.ht, t.b);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -307,14 +470,21 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs0,
 #pragma unroll
           for (int kk = 0; kk < DS / 16; ++kk)
             umma_f16_ss(d, kmajor_desc(a_s, kk), kmajor_desc(b_s, kk), id_s, kk > 0);
+          if (kTeacher) {
 #pragma unroll
-          for (int kk = 0; kk < DT / 16; ++kk)
-            umma_f16_ss(d + 128, kmajor_desc(a_t, kk), kmajor_desc(b_t, kk), id_t, kk > 0);
+            for (int kk = 0; kk < DT / 16; ++kk)
+              umma_f16_ss(d + 128, kmajor_desc(a_t, kk), kmajor_desc(b_t, kk), id_t, kk > 0);
+          }
           umma_commit(&misc->k_empty[s]);
           umma_commit(&misc->s_full[bf]);
         }
       }
     }
+  } else if (warp < kRowWarps && MODE == 0) {
+    forward_rows_lse<L>(misc, stat, p, t, bits, lse_s, tmem, warp, lane, abort, err);
+  } else if (warp < kRowWarps && MODE == 2) {
+    forward_rows_kl_given_lse<L>(misc, stat, p, t, bits, lse_s, lse_t, partials, tmem, warp,
+                                 lane, abort, err);
   } else if (warp < kRowWarps) {
     // ---------------- row warps: warpgroup wg owns columns [32 wg, 32 wg + 32) of each tile
     const int wg = warp >> 2, q = warp & 3;
@@ -1084,12 +1254,12 @@ bool build_maps(Maps& m, const Problem& p, const void* qs, const void* ks, const
          make_map(&m.kt, kt, p.dtype_t, p.Dt, p.T, p.Hkv_t, p.B, s3);
 }
 
-template <int DS, int DT>
+template <int DS, int DT, int MODE = 1>
 cudaError_t run_forward(const Problem& p, const Maps& m, const uint32_t* bits, float* lse_s,
                         float* lse_t, float* partials, int grid, const GroupRef& gref,
                         cudaStream_t st) {
   using L = FwdLayout<DS, DT>;
-  auto k = sm100_forward_kernel<DS, DT>;
+  auto k = sm100_forward_kernel<DS, DT, MODE>;
   cudaError_t e = prep(k, L::BYTES);
   if (e != cudaSuccess) return e;
   k<<<grid, kThreads, L::BYTES, st>>>(m.qs, m.ks, m.qt, m.kt, p, bits, lse_s, lse_t, partials,
@@ -1328,16 +1498,29 @@ bool build_group(const Problem& base, const GroupSpec* g, int n, std::vector<uin
   return true;
 }
 
+template <int MODE>
+cudaError_t dispatch_forward_mode(const Problem& p, const Maps& m, const uint32_t* bits,
+                                  float* lse_s, float* lse_t, float* partials, int grid,
+                                  const GroupRef& g, cudaStream_t st) {
+  if (MODE == 0) {  // the student pair only
+    if (p.Ds == 128) return run_forward<128, 128, 0>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
+    return run_forward<64, 64, 0>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
+  }
+  if (p.Ds == 128 && p.Dt == 128)
+    return run_forward<128, 128, MODE>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
+  if (p.Ds == 64 && p.Dt == 64)
+    return run_forward<64, 64, MODE>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
+  if (p.Ds == 128 && p.Dt == 64)
+    return run_forward<128, 64, MODE>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
+  return run_forward<64, 128, MODE>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
+}
+
 cudaError_t dispatch_forward(const Problem& p, const Maps& m, const uint32_t* bits, float* lse_s,
                              float* lse_t, float* partials, int grid, const GroupRef& g,
-                             cudaStream_t st) {
-  if (p.Ds == 128 && p.Dt == 128)
-    return run_forward<128, 128>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
-  if (p.Ds == 64 && p.Dt == 64)
-    return run_forward<64, 64>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
-  if (p.Ds == 128 && p.Dt == 64)
-    return run_forward<128, 64>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
-  return run_forward<64, 128>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
+                             cudaStream_t st, int mode = 1) {
+  if (mode == 0) return dispatch_forward_mode<0>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
+  if (mode == 2) return dispatch_forward_mode<2>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
+  return dispatch_forward_mode<1>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
 }
 
 cudaError_t dispatch_grad(const Problem& p, const Maps& m, const std::vector<Chunk>& plan,
@@ -1368,12 +1551,12 @@ int sm100_num_partials(const Problem& p) { return p.B * p.Hq * ((p.T + kBM - 1) 
 cudaError_t launch_sm100_forward(const Problem& p, const void* qs, const void* ks,
                                  const void* qt, const void* kt, const TensorStrides* strides,
                                  const uint32_t* bits, float* lse_s, float* lse_t,
-                                 float* partials, int* num_partials, cudaStream_t st) {
+                                 float* partials, int* num_partials, cudaStream_t st, int mode) {
   Maps m;
   if (!build_maps(m, p, qs, ks, qt, kt, strides)) return cudaErrorInvalidValue;
   const int grid = sm100_num_partials(p);
   if (num_partials) *num_partials = grid;
-  return dispatch_forward(p, m, bits, lse_s, lse_t, partials, grid, GroupRef{}, st);
+  return dispatch_forward(p, m, bits, lse_s, lse_t, partials, grid, GroupRef{}, st, mode);
 }
 
 bool sm100_backward_supports(const Problem& p) {

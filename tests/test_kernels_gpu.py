@@ -16,13 +16,20 @@ pytestmark = pytest.mark.gpu
 TC_DIMS = (64, 128)
 
 
+@pytest.mark.parametrize("generic", [False, True], ids=["auto", "generic"])
 @pytest.mark.parametrize("case", C.lse_cases(), ids=lambda c: c.name)
-def test_lse_matches_reference(case, golden):
+def test_lse_matches_reference(case, generic, golden):
+    """kernel_A level: the tensor-core LSE-only launch for head dims 64 and
+    128, the CUDA-core kernel for the others (and when forced)."""
     from linearard_b200.attention_KL import lse_stats
     q, k, mask = C.make_lse_inputs(case)
-    out = lse_stats(cuda(q), cuda(k), attn_mask=cuda(mask), causal=case.causal,
-                    sm_scale=C.sm_scale(case.D))
+    with force_generic(generic):
+        out = lse_stats(cuda(q), cuda(k), attn_mask=cuda(mask), causal=case.causal,
+                        sm_scale=C.sm_scale(case.D))
+        used_tc = path_is_tensor_core()
     torch.cuda.synchronize()
+    check_device_status()
+    assert used_tc == ((not generic) and case.D in TC_DIMS)
     rtol, atol = REF_TOL[case.dtype]
     ref = torch.from_numpy(golden[f"{case.name}/lse"])
     torch.testing.assert_close(out.cpu(), ref, rtol=rtol, atol=atol)
@@ -62,8 +69,10 @@ def test_forward_backward_match_reference(case, generic, golden):
     # kernel-B level: KL from the reference's own LSEs
     lse_ref_s = torch.from_numpy(g["lse_s"]).cuda()
     lse_ref_t = torch.from_numpy(g["lse_t"]).cuda()
-    kl_b = kl_forward(*Q[:2], lse_ref_s, *Q[2:], lse_ref_t, attn_mask=m, causal=case.causal,
-                      sm_scale_s=sc_s, sm_scale_t=sc_t)
+    with force_generic(generic):
+        kl_b = kl_forward(*Q[:2], lse_ref_s, *Q[2:], lse_ref_t, attn_mask=m, causal=case.causal,
+                          sm_scale_s=sc_s, sm_scale_t=sc_t)
+        assert path_is_tensor_core() == expect_tc
     assert_loss_close(float(kl_b), float(g["kl"]))
 
 
@@ -124,3 +133,42 @@ def test_mask_dtypes_and_cpu_mask(mdtype):
     assert_grad_close(dq.cpu().numpy(), rdq, "dq")
     assert_grad_close(dk.cpu().numpy(), rdk, "dk")
     assert np.all(dq.cpu().numpy()[1, :, 150:] == 0.0)
+
+
+@pytest.mark.parametrize("D", TC_DIMS)
+@pytest.mark.parametrize("T", [1, 129, 383, 1000])
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("masked", [False, True])
+def test_tensor_core_lse_and_kl_given_lse_vs_oracle(D, T, causal, masked):
+    """The kernel-A / kernel-B level entry points on the tensor cores: ragged
+    T, GQA, padding masks (including a padded first token, whose row has no
+    valid column under the causal mask), against the oracle."""
+    from linearard_b200.attention_KL import kl_forward, lse_stats
+    gen = torch.Generator().manual_seed(T * 13 + D + (7 if masked else 0))
+    B, Hq, Hkv = 2, 4, 2
+    qs = torch.randn(B, Hq, T, D, generator=gen).bfloat16()
+    ks = torch.randn(B, Hkv, T, D, generator=gen).bfloat16()
+    qt = (qs.float() + 0.2 * torch.randn(B, Hq, T, D, generator=gen)).bfloat16()
+    kt = torch.randn(B, Hq, T, D, generator=gen).bfloat16()
+    mask = None
+    if masked:
+        mask = (torch.rand(B, T, generator=gen) > 0.25).to(torch.int32)
+        mask[:, 0] = 0
+    a = [C.to_np(x) for x in (qs, ks, qt, kt)]
+    m_np = None if mask is None else C.to_np(mask)
+    ref_ls = O.oracle_lse(a[0], a[1], m_np, causal)
+    ref_lt = O.oracle_lse(a[2], a[3], m_np, causal)
+    ls = lse_stats(qs.cuda(), ks.cuda(), attn_mask=cuda(mask), causal=causal)
+    assert path_is_tensor_core()
+    lt = lse_stats(qt.cuda(), kt.cuda(), attn_mask=cuda(mask), causal=causal)
+    torch.cuda.synchronize()
+    check_device_status()
+    np.testing.assert_allclose(ls.cpu().numpy(), ref_ls, rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(lt.cpu().numpy(), ref_lt, rtol=1e-4, atol=1e-4)
+    # KL given the oracle's LSEs (-inf rows included)
+    kl = kl_forward(qs.cuda(), ks.cuda(), torch.from_numpy(ref_ls).float().cuda(), qt.cuda(),
+                    kt.cuda(), torch.from_numpy(ref_lt).float().cuda(), attn_mask=cuda(mask),
+                    causal=causal)
+    assert path_is_tensor_core()
+    ref_kl = O.oracle_kl(a[0], a[1], ref_ls, a[2], a[3], ref_lt, m_np, causal)
+    assert_loss_close(float(kl), ref_kl)
