@@ -366,9 +366,6 @@ int32_t backward_impl(const void* qs, const void* ks, const float* lse_s, const 
                                    dloss, dq, dk, alias, lsc_ptr(p, mask, ws),
                                    static_cast<uint8_t*>(ws) + base, ws_bytes - base, st);
   } else {
-    // dk (and dq when it is the same buffer) accumulates with atomics
-    const size_t dk_bytes = (size_t)p->B * p->Hkv_s * p->T * p->Ds * sizeof(float);
-    if (cudaMemsetAsync(dk, 0, dk_bytes, st) != cudaSuccess) return LKL_ERR_LAUNCH;
     t_last_path = 0;
     e = lkl::launch_generic_backward(q, qs, ks, lse_s, qt, kt, lse_t, bits, dloss, dq, dk, alias,
                                      st);

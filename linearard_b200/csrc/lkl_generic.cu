@@ -4,8 +4,10 @@
 // alignment; the sm_100a tensor-core kernels (lkl_sm100.cu) take the shapes
 // they support.  Both compute the same quantities:
 //   forward  -- row LSEs (kernel_A.py:146-158) and the KL sum (kernel_B.py:206-218),
-//   backward -- dq = sc*D.Ks, dk = sc*D^T.Qs with D = ps - pt rounded to the
-//               input dtype (kernel_C.py:224-253).
+//   backward -- dq = sc*D.Ks (row-stationary launch), dk = sc*D^T.Qs
+//               (column-stationary launch that recomputes D), with D = ps - pt
+//               rounded to the input dtype (kernel_C.py:224-253); each
+//               gradient row has one writer, so results are bit-reproducible.
 //
 // Tiling: a 256-thread block owns 32 rows of one (batch, head) and walks
 // 32-column tiles (only those at or below the diagonal when causal).  Thread t
@@ -249,11 +251,11 @@ generic_forward_kernel(Problem p, const void* __restrict__ qs, const void* __res
 
 // ---------------------------------------------------------------- backward
 __global__ void __launch_bounds__(kGThreads)
-generic_backward_kernel(Problem p, const void* __restrict__ qs, const void* __restrict__ ks,
+generic_dq_kernel(Problem p, const void* __restrict__ qs, const void* __restrict__ ks,
                         const float* __restrict__ lse_s, const void* __restrict__ qt,
                         const void* __restrict__ kt, const float* __restrict__ lse_t,
                         const uint32_t* __restrict__ bits, const float* __restrict__ dloss,
-                        float* dq, float* dk, int alias) {
+                        float* dq) {
   extern __shared__ float smem[];
   const int Ds = p.Ds, Dt = p.Dt, T = p.T;
   float* sQs = smem;
@@ -325,28 +327,119 @@ generic_backward_kernel(Problem p, const void* __restrict__ qs, const void* __re
         dqacc[kk] += a;
       }
     }
-    // dk[j][d] += sum_r D[r][c] * Qs[r][d] for this tile's columns
-    {
-      const int c = threadIdx.x >> 3, j = j0 + c;
-      if (j < T) {
-        float* dst = dk + (((size_t)b * p.Hkv_s + hs) * T + j) * Ds;
-        for (int kk = 0; kk < nd; ++kk) {
-          const int d = sub + 8 * kk;
-          float a = 0.f;
-          for (int rr = 0; rr < kGBM; ++rr) a = fmaf(sD[rr * (kGBN + 1) + c], sQs[rr * (Ds + 1) + d], a);
-          if (a != 0.f) atomicAdd(dst + d, a * gscale);
-        }
-      }
-    }
   }
   if (row_in) {
     float* dst = dq + (((size_t)b * p.Hq + h) * T + i) * Ds;
 #pragma unroll
+    for (int kk = 0; kk < 32; ++kk)
+      if (kk < nd) dst[sub + 8 * kk] = row_ok ? dqacc[kk] * gscale : 0.f;
+  }
+}
+
+// dk launch (column-stationary, deterministic): a block owns 32 key columns j
+// of one (batch, student kv head) and walks the query rows of every query
+// head of that kv group (rows i >= j when causal), recomputing D for its
+// columns; dk[j][d] = sc * sum_i D[i][j] Qs[i][d] is written once by its
+// owner block (added to what the dq launch wrote when dq and dk share a
+// buffer), so no float atomics are involved.
+__global__ void __launch_bounds__(kGThreads)
+generic_dk_kernel(Problem p, const void* __restrict__ qs, const void* __restrict__ ks,
+                  const float* __restrict__ lse_s, const void* __restrict__ qt,
+                  const void* __restrict__ kt, const float* __restrict__ lse_t,
+                  const uint32_t* __restrict__ bits, const float* __restrict__ dloss, float* dk,
+                  int alias) {
+  extern __shared__ float smem[];
+  const int Ds = p.Ds, Dt = p.Dt, T = p.T;
+  float* sQs = smem;
+  float* sKs = sQs + kGBM * (Ds + 1);
+  float* sQt = sKs + kGBN * (Ds + 1);
+  float* sKt = sQt + kGBM * (Dt + 1);
+  float* sD = sKt + kGBN * (Dt + 1);  // [kGBM][kGBN + 1]
+  __shared__ float sLs[kGBM], sLt[kGBM];
+  __shared__ int sOk[kGBM];
+
+  const int n_ct = (T + kGBN - 1) / kGBN;
+  const int bg = blockIdx.x / n_ct;             // b * Hkv_s + hs
+  const int ct = n_ct - 1 - (int)(blockIdx.x % n_ct);
+  const int b = bg / p.Hkv_s, hs = bg % p.Hkv_s;
+  const int G = p.Hq / p.Hkv_s;
+  const int words = (T + 31) / 32;
+  const int j0 = ct * kGBN;
+  const float gscale = p.sc_s * (dloss ? *dloss : 1.f);
+  const size_t k_off_s = ((size_t)b * p.Hkv_s + hs) * T * Ds;
+  load_tile(sKs, ks, k_off_s, j0, T, Ds, p.dtype_s);
+
+  const int r = threadIdx.x >> 3, sub = threadIdx.x & 7;  // D: row r, columns sub + 8k
+  const int cc = threadIdx.x >> 3;                          // dk: column cc, d = sub + 8kk
+  const int nd = Ds / 8 > 0 ? Ds / 8 : 1;
+  float dkacc[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) dkacc[k] = 0.f;
+
+  const int n_mt = (T + kGBM - 1) / kGBM;
+  const int mt0 = p.causal ? j0 / kGBM : 0;
+  int ht_loaded = -1;
+  for (int g = 0; g < G; ++g) {
+    const int h = hs * G + g;
+    const int ht = h / (p.Hq / p.Hkv_t);
+    const size_t q_off_s = ((size_t)b * p.Hq + h) * T * Ds;
+    const size_t q_off_t = ((size_t)b * p.Hq + h) * T * Dt;
+    const size_t row_off = ((size_t)b * p.Hq + h) * T;
+    for (int mt = mt0; mt < n_mt; ++mt) {
+      __syncthreads();
+      if (ht != ht_loaded) load_tile(sKt, kt, ((size_t)b * p.Hkv_t + ht) * T * Dt, j0, T, Dt,
+                                     p.dtype_t);
+      load_tile(sQs, qs, q_off_s, mt * kGBM, T, Ds, p.dtype_s);
+      load_tile(sQt, qt, q_off_t, mt * kGBM, T, Dt, p.dtype_t);
+      if (threadIdx.x < kGBM) {
+        const int i = mt * kGBM + threadIdx.x;
+        float Ls = 0.f, Lt = 0.f;
+        bool ok = i < T && token_valid(bits, words, b, i);
+        if (i < T) {
+          Ls = lse_s[row_off + i];
+          Lt = lse_t[row_off + i];
+          ok = ok && isfinite(Ls) && isfinite(Lt);
+        }
+        sLs[threadIdx.x] = Ls;
+        sLt[threadIdx.x] = Lt;
+        sOk[threadIdx.x] = ok ? 1 : 0;
+      }
+      __syncthreads();
+      ht_loaded = ht;
+      const int i = mt * kGBM + r;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int c = sub + 8 * k, j = j0 + c;
+        const bool ok = sOk[r] && j < T && (!p.causal || j <= i) && token_valid(bits, words, b, j);
+        float dv = 0.f;
+        if (ok) {
+          const float xs = dot_rows(sQs + r * (Ds + 1), sKs + c * (Ds + 1), Ds) * p.sc_s;
+          const float xt = dot_rows(sQt + r * (Dt + 1), sKt + c * (Dt + 1), Dt) * p.sc_t;
+          dv = round_to_dtype(__expf(xs - sLs[r]) - __expf(xt - sLt[r]), p.dtype_s);
+        }
+        sD[r * (kGBN + 1) + c] = dv;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int kk = 0; kk < 32; ++kk) {
+        if (kk < nd) {
+          const int d = sub + 8 * kk;
+          float a = 0.f;
+          for (int rr = 0; rr < kGBM; ++rr)
+            a = fmaf(sD[rr * (kGBN + 1) + cc], sQs[rr * (Ds + 1) + d], a);
+          dkacc[kk] += a;
+        }
+      }
+    }
+  }
+  const int j = j0 + cc;
+  if (j < T) {
+    float* dst = dk + (((size_t)b * p.Hkv_s + hs) * T + j) * Ds;
+#pragma unroll
     for (int kk = 0; kk < 32; ++kk) {
       if (kk < nd) {
-        const float v = row_ok ? dqacc[kk] * gscale : 0.f;
-        if (alias) atomicAdd(dst + sub + 8 * kk, v);
-        else dst[sub + 8 * kk] = v;
+        const float v = dkacc[kk] * gscale;
+        dst[sub + 8 * kk] = alias ? dst[sub + 8 * kk] + v : v;
       }
     }
   }
@@ -428,12 +521,18 @@ cudaError_t launch_generic_backward(const Problem& p, const void* qs, const void
                                     const float* lse_t, const uint32_t* bits,
                                     const float* dloss, float* dq, float* dk, bool alias,
                                     cudaStream_t st) {
-  const int grid = generic_num_partials(p);
+  // dq rows first (plain stores), then dk rows (stored, or added to the dq
+  // rows when both are one buffer): every row has one writer per launch
   const size_t smem = bwd_smem(p);
-  cudaError_t e = set_smem(generic_backward_kernel, smem);
+  cudaError_t e = set_smem(generic_dq_kernel, smem);
+  if (e == cudaSuccess) e = set_smem(generic_dk_kernel, smem);
   if (e != cudaSuccess) return e;
-  generic_backward_kernel<<<grid, kGThreads, smem, st>>>(p, qs, ks, lse_s, qt, kt, lse_t, bits,
-                                                        dloss, dq, dk, alias ? 1 : 0);
+  generic_dq_kernel<<<generic_num_partials(p), kGThreads, smem, st>>>(p, qs, ks, lse_s, qt, kt,
+                                                                      lse_t, bits, dloss, dq);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  const int grid_k = p.B * p.Hkv_s * ((p.T + kGBN - 1) / kGBN);
+  generic_dk_kernel<<<grid_k, kGThreads, smem, st>>>(p, qs, ks, lse_s, qt, kt, lse_t, bits, dloss,
+                                                     dk, alias ? 1 : 0);
   return cudaGetLastError();
 }
 
