@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--cpu-sample-n", type=int, default=2048)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-numa", action="store_true",
+                    help="leave the pinned staging buffers wherever the allocator puts them")
     return ap.parse_args()
 
 
@@ -443,7 +445,7 @@ def main():
         # (the loss is a sum over heads).  All copies go out on a copy stream at
         # the start of the step; the forward of slice k waits only for slice k's
         # copy, so the PCIe transfer of later slices runs under earlier compute.
-        numa = gpu_local_cpus(dev)
+        numa = None if args.no_numa else gpu_local_cpus(dev)
         saved_affinity = None
         if numa:
             # pinned staging pages are placed on the NUMA node of this GPU's
