@@ -67,7 +67,7 @@ def _timed(arms, warmup, iters):
         e1.record()
         torch.cuda.synchronize()
         out[name] = e0.elapsed_time(e1) / iters
-        out[name.replace("_ms", "_loss")] = float(loss)
+        out[name.replace("_ms", "_loss")] = float(loss.detach())
     return out
 
 
