@@ -103,7 +103,7 @@ size_t lkl_forward_workspace_size(const lkl_problem* p, int32_t has_mask);
 size_t lkl_workspace_size(const lkl_problem* p, int32_t has_mask);
 
 /* Bytes of scratch lkl_backward needs: lkl_workspace_size plus, for the
- * tensor-core path (Ds, Dt in {64, 128}), a buffer for the
+ * tensor-core path (Ds, Dt in {8, 16, 32, 64, 128}), a buffer for the
  * 16-bit D tiles (p_s - p_t) that the dq pass hands to the dk pass: all of
  * them up to 8 GiB, beyond that the backward runs in chunks of kv heads or of
  * query-tile ranges (so the buffer stays bounded for any T).  A multiple of
@@ -160,7 +160,7 @@ int32_t lkl_backward(const void* qs, const void* ks, const float* lse_s,
  * tensors are read in place through TMA, so no copy is made.
  * Requirements: every stride a positive multiple of 8 elements and every base
  * pointer 16-byte aligned (LKL_ERR_MISALIGNED otherwise); the tensor-core path
- * (sm_100, Ds and Dt in {64, 128}), LKL_ERR_UNSUPPORTED otherwise.  Outputs (lse, loss, dq, dk) are contiguous,
+ * (sm_100, Ds and Dt in {8, 16, 32, 64, 128}), LKL_ERR_UNSUPPORTED otherwise.  Outputs (lse, loss, dq, dk) are contiguous,
  * as in lkl_forward / lkl_backward; everything else is the same.
  * `strides` points to 4 entries: qs, ks, qt, kt. */
 typedef struct lkl_strides {
@@ -187,7 +187,7 @@ int32_t lkl_backward_strided(const void* qs, const void* ks, const float* lse_s,
  * `shared` gives what the items have in common (B, T, Ds, Dt, dtypes, causal,
  * mask dtype, scales; its Hq / Hkv_s / Hkv_t are ignored); the mask is shared.
  * Every item must be on the tensor-core path (16-byte-aligned inputs,
- * contiguous or strided, Ds and Dt in {64, 128}), else LKL_ERR_UNSUPPORTED.  At most LKL_MAX_GROUP_ITEMS items (LKL_ERR_TOO_LARGE).
+ * contiguous or strided, Ds and Dt in {8, 16, 32, 64, 128}), else LKL_ERR_UNSUPPORTED.  At most LKL_MAX_GROUP_ITEMS items (LKL_ERR_TOO_LARGE).
  * The item table (tensor maps and pointers, 576 B per item) goes to the device
  * inside the call through a pinned host ring that the library allocates once
  * (8 MiB, the only host allocation it makes), so the call does not wait for

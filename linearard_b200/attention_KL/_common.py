@@ -16,6 +16,8 @@ import torch
 from .. import _lib
 
 SUPPORTED_HEAD_DIMS = (8, 16, 32, 64, 128, 256)
+# head dims of the sm_100a tensor-core kernels (8..32 run zero-padded to 64)
+TC_HEAD_DIMS = (8, 16, 32, 64, 128)
 
 _DT = {torch.float16: _lib.LKL_F16, torch.bfloat16: _lib.LKL_BF16}
 _MASK_DT = {torch.bool: _lib.LKL_MASK_BOOL, torch.uint8: _lib.LKL_MASK_U8,

@@ -14,7 +14,7 @@ has its own head counts.  Inputs may be [B, H, T, D] views with any strides
 that are multiples of 8 elements (the transposed projections an attention
 hook sees): they are read in place, as by ``attn_kl_align_strided``.  When an
 item is outside the tensor-core path (16-byte-aligned inputs, Ds and Dt in
-{64, 128}) the call falls back to per-item
+{8, 16, 32, 64, 128}) the call falls back to per-item
 ``attn_kl_align_strided`` calls.
 """
 from __future__ import annotations

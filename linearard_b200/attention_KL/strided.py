@@ -12,7 +12,7 @@ are: the tensor-core kernels read them in place through 4-D TMA maps
 Same value, gradients and call signature as ``attn_kl_align``.  Inputs need a
 last-dim stride of 1, the other strides multiples of 8 elements and 16-byte
 aligned storage; shapes the tensor-core path does not cover (Ds or Dt not in
-{64, 128}, other strides) go through ``attn_kl_align`` on contiguous copies,
+{8, 16, 32, 64, 128}, other strides) go through ``attn_kl_align`` on contiguous copies,
 i.e. the same GPU kernels the reference-shaped call uses.
 """
 from __future__ import annotations
@@ -22,7 +22,7 @@ import ctypes
 import torch
 
 from .. import _lib
-from ._common import prepare_mask, problem, ptr, stream_of, workspace
+from ._common import TC_HEAD_DIMS, prepare_mask, problem, ptr, stream_of, workspace
 from .integration import attn_kl_align
 
 __all__ = ["attn_kl_align_strided", "AttnKLAlignStridedFn", "strided_ok"]
@@ -43,7 +43,7 @@ def strided_ok(qs, ks, qt, kt) -> bool:
     if qs.dtype not in (torch.float16, torch.bfloat16) or qt.dtype not in (torch.float16,
                                                                             torch.bfloat16):
         return False
-    return (qs.shape[3] in (64, 128) and qt.shape[3] in (64, 128)
+    return (qs.shape[3] in TC_HEAD_DIMS and qt.shape[3] in TC_HEAD_DIMS
             and qs.shape[1] % ks.shape[1] == 0 and qs.shape[1] % kt.shape[1] == 0)
 
 

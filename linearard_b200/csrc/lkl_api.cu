@@ -172,7 +172,7 @@ const char* lkl_status_string(int32_t s) {
     case LKL_ERR_TOO_LARGE: return "problem exceeds the supported size";
     case LKL_ERR_UNSUPPORTED:
       return "strided or grouped inputs need the tensor-core path (sm_100, Ds and Dt in "
-             "{64, 128}, 16-byte aligned)";
+             "{8, 16, 32, 64, 128}, 16-byte aligned)";
     default: return "unknown status";
   }
 }

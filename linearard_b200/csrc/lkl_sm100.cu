@@ -696,7 +696,7 @@ __global__ void scale_lse_kernel(const float* __restrict__ lse_s, const float* _
 // the row's only owner).
 template <int NC>
 __device__ __forceinline__ void store_rows(uint32_t taddr, float* row_ptr, float scale,
-                                           bool do_store, bool accumulate) {
+                                           bool do_store, bool accumulate, int n_valid = NC) {
   constexpr int W = NC < 32 ? NC : 32;
 #pragma unroll
   for (int c = 0; c < NC; c += W) {
@@ -707,6 +707,8 @@ __device__ __forceinline__ void store_rows(uint32_t taddr, float* row_ptr, float
     if (do_store) {
 #pragma unroll
       for (int k = 0; k < W; k += 4) {
+        // head dims below 64 run zero-padded to 64: only the real columns exist
+        if (c + k >= n_valid) break;
         float4* dst = reinterpret_cast<float4*>(row_ptr + c + k);
         float4 f = make_float4(v[k] * scale, v[k + 1] * scale, v[k + 2] * scale, v[k + 3] * scale);
         if (accumulate) {
@@ -978,9 +980,9 @@ sm100_dq_kernel(const __grid_constant__ CUtensorMap tm_qs0,
     }
     if (n_steps > 0 && mbar_wait(&misc->d_empty, (n_steps - 1) & 1, abort, err)) {
       tc_fence_after();
-      float* row = out + ((size_t)bh * p.T + own) * DS;
-      store_rows<DS / 4>(lane_addr + kColAcc + wg * (DS / 4), row + wg * (DS / 4), gscale, own_in,
-                         c.dq_acc != 0);
+      float* row = out + ((size_t)bh * p.T + own) * p.Ds;
+      store_rows<DS / 4>(lane_addr + kColAcc + wg * (DS / 4), row + wg * (DS / 4), gscale,
+                         own_in && wg * (DS / 4) < p.Ds, c.dq_acc != 0, p.Ds - wg * (DS / 4));
     }
   }
 
@@ -1172,9 +1174,9 @@ sm100_dk_kernel(const __grid_constant__ CUtensorMap tm_qs0, const Problem p0, co
       const float gscale = k.p.sc_s * (dloss ? *dloss : 1.f);
       // the first chunk that reaches key tile j stores, later ones add
       const bool accumulate = alias != 0 || (k.p.causal ? k.j < c.i0 : c.i0 > 0);
-      float* row = out + (((size_t)k.b * k.p.Hkv_s + k.hs) * k.p.T + own) * DS;
+      float* row = out + (((size_t)k.b * k.p.Hkv_s + k.hs) * k.p.T + own) * k.p.Ds;
       store_rows<DS>(tmem + ab * 128 + ((uint32_t)(q * 32) << 16), row, gscale, own < k.p.T,
-                     accumulate);
+                     accumulate, k.p.Ds);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&misc->s_empty[ab]);
@@ -1212,6 +1214,9 @@ EncodeTiledFn get_encoder() {
 // A [B][H][T][D] 16-bit tensor with element strides (sb, sh, st; d stride 1)
 // viewed as a 4-D map {D, T, H, B} with a {64, 128, 1, 1} box.  Rows past T
 // read as zeros.
+// Head dim the tensor-core kernels are instantiated for: 64 for 8..64, else 128.
+int tc_dim(int d) { return d <= 64 ? 64 : 128; }
+
 bool make_map(CUtensorMap* m, const void* ptr, int dtype, int D, int T, int H, int B,
               const TensorStrides& s) {
   EncodeTiledFn enc = get_encoder();
@@ -1503,14 +1508,14 @@ cudaError_t dispatch_forward_mode(const Problem& p, const Maps& m, const uint32_
                                   float* lse_s, float* lse_t, float* partials, int grid,
                                   const GroupRef& g, cudaStream_t st) {
   if (MODE == 0) {  // the student pair only
-    if (p.Ds == 128) return run_forward<128, 128, 0>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
+    if (tc_dim(p.Ds) == 128) return run_forward<128, 128, 0>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
     return run_forward<64, 64, 0>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
   }
-  if (p.Ds == 128 && p.Dt == 128)
+  if (tc_dim(p.Ds) == 128 && tc_dim(p.Dt) == 128)
     return run_forward<128, 128, MODE>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
-  if (p.Ds == 64 && p.Dt == 64)
+  if (tc_dim(p.Ds) == 64 && tc_dim(p.Dt) == 64)
     return run_forward<64, 64, MODE>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
-  if (p.Ds == 128 && p.Dt == 64)
+  if (tc_dim(p.Ds) == 128 && tc_dim(p.Dt) == 64)
     return run_forward<128, 64, MODE>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
   return run_forward<64, 128, MODE>(p, m, bits, lse_s, lse_t, partials, grid, g, st);
 }
@@ -1527,11 +1532,11 @@ cudaError_t dispatch_grad(const Problem& p, const Maps& m, const std::vector<Chu
                           const float2* lsc, const uint32_t* bits, const float* dloss, float* dq,
                           float* dk, bool alias, uint16_t* dbuf, const GroupRef& g,
                           cudaStream_t st) {
-  if (p.Ds == 128 && p.Dt == 128)
+  if (tc_dim(p.Ds) == 128 && tc_dim(p.Dt) == 128)
     return run_grad<128, 128>(p, m, plan, lsc, bits, dloss, dq, dk, alias, dbuf, g, st);
-  if (p.Ds == 64 && p.Dt == 64)
+  if (tc_dim(p.Ds) == 64 && tc_dim(p.Dt) == 64)
     return run_grad<64, 64>(p, m, plan, lsc, bits, dloss, dq, dk, alias, dbuf, g, st);
-  if (p.Ds == 128 && p.Dt == 64)
+  if (tc_dim(p.Ds) == 128 && tc_dim(p.Dt) == 64)
     return run_grad<128, 64>(p, m, plan, lsc, bits, dloss, dq, dk, alias, dbuf, g, st);
   return run_grad<64, 128>(p, m, plan, lsc, bits, dloss, dq, dk, alias, dbuf, g, st);
 }
@@ -1539,8 +1544,11 @@ cudaError_t dispatch_grad(const Problem& p, const Maps& m, const std::vector<Chu
 }  // namespace
 
 bool sm100_shape_ok(const Problem& p) {
-  const bool ds_ok = p.Ds == 64 || p.Ds == 128;
-  const bool dt_ok = p.Dt == 64 || p.Dt == 128;
+  // 8, 16 and 32 run as 64 with the tensor maps' zero fill beyond D (the
+  // padded columns add nothing to the scores and are never stored)
+  auto ok = [](int d) { return d == 8 || d == 16 || d == 32 || d == 64 || d == 128; };
+  const bool ds_ok = ok(p.Ds);
+  const bool dt_ok = ok(p.Dt);
   return ds_ok && dt_ok && p.sc_s > 0.f && p.sc_t > 0.f && p.T >= 1;
 }
 

@@ -80,7 +80,7 @@ def test_backward_workspace_holds_the_d_tiles():
         assert (L.lkl_backward_workspace_size(ctypes.byref(nc), mask)
                 == L.lkl_workspace_size(ctypes.byref(nc), mask) + 4 * n_t * n_t * 32768)
     # shapes served by the CUDA-core kernels need nothing extra
-    for kw in (dict(Ds=32, Dt=32, Hkv_t=2), dict(Ds=256, Dt=128)):   # head dims 32 and 256
+    for kw in (dict(Ds=256, Dt=256, Hkv_t=2), dict(Ds=256, Dt=128)):   # head dim 256
         p = _prob(**kw)
         assert (L.lkl_backward_workspace_size(ctypes.byref(p), 0)
                 == L.lkl_workspace_size(ctypes.byref(p), 0))
@@ -220,8 +220,8 @@ def test_grouped_entry_points_validate_before_device():
     assert n_f > 0 and n_f % 256 == 0
     n_t = (300 + 127) // 128
     assert n_b - n_f >= 4 * n_t * (n_t + 1) // 2 * 32768   # every D tile fits (< 8 GiB)
-    # head dim 32 is outside the tensor-core path
-    small = _prob(Ds=32, Dt=32, Hkv_t=2)
+    # head dim 256 is outside the tensor-core path
+    small = _prob(Ds=256, Dt=256, Hkv_t=2)
     assert L.lkl_grouped_workspace_size(1, one, ctypes.byref(small), 0, 0) == 0
     c = ctypes.c_void_p
     assert L.lkl_forward_grouped(1, one, None, ctypes.byref(small), c(fake), c(fake), 1 << 20,
@@ -271,4 +271,4 @@ def test_backward_plan_chunks():
     # below one query-tile row of tiles: refused
     assert _plan(p, base + (n_t - 1) * 32768)[0] == 6
     # the CUDA-core shapes have no D buffer and no chunks
-    assert _plan(_prob(Ds=32, Dt=32)) == (0, 0)
+    assert _plan(_prob(Ds=256, Dt=256)) == (0, 0)

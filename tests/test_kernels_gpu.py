@@ -13,7 +13,7 @@ from oracle import attn_kl_oracle as O
 
 pytestmark = pytest.mark.gpu
 
-TC_DIMS = (64, 128)
+TC_DIMS = (8, 16, 32, 64, 128)   # head dims on the tensor cores
 
 
 @pytest.mark.parametrize("generic", [False, True], ids=["auto", "generic"])
@@ -77,7 +77,7 @@ def test_forward_backward_match_reference(case, generic, golden):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("D", TC_DIMS)
+@pytest.mark.parametrize("D", (32, 64, 128))
 @pytest.mark.parametrize("T", [1, 127, 128, 129, 383, 640])
 @pytest.mark.parametrize("causal", [True, False])
 def test_tensor_core_vs_oracle_tile_edges(D, T, causal, dtype):
@@ -174,7 +174,7 @@ def test_tensor_core_lse_and_kl_given_lse_vs_oracle(D, T, causal, masked):
     assert_loss_close(float(kl), ref_kl)
 
 
-@pytest.mark.parametrize("D", [32, 256])
+@pytest.mark.parametrize("D", [256])
 def test_cuda_core_backward_is_bit_reproducible(D):
     """Head dims outside the tensor-core kernels: the CUDA-core backward writes
     each dq and dk row once (a dq launch, then a column-stationary dk launch),
