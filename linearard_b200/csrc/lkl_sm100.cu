@@ -266,7 +266,7 @@ __device__ __forceinline__ void forward_rows_lse(Misc* misc, float* stat, const 
     __syncwarp();
     if (lane == 0) mbar_arrive(&misc->s_empty[bf]);
     if (!row_valid) continue;
-    const int c0 = j * kBN + wg * 32;
+    const int c0 = (t.n_ct - 1 - j) * kBN + wg * 32;
     if (!((c0 + 31 <= lim) && (bits == nullptr))) {
 #pragma unroll
       for (int k = 0; k < 32; ++k)
@@ -278,7 +278,7 @@ __device__ __forceinline__ void forward_rows_lse(Misc* misc, float* stat, const 
     mx = fmaxf(mx, x[31]);
     if (mx < -1.0e29f) continue;
     const float ms_new = fmaxf(m_s, mx * cs);
-    l_s *= ex2(m_s - ms_new);
+    if (__any_sync(__activemask(), ms_new > m_s)) l_s *= ex2(m_s - ms_new);
     const uint64_t nms2 = f2pack(-ms_new, -ms_new);
     uint64_t ls2 = 0;
 #pragma unroll
@@ -355,7 +355,7 @@ __device__ __forceinline__ void forward_rows_kl_given_lse(
     __syncwarp();
     if (lane == 0) mbar_arrive(&misc->s_empty[bf]);
     if (!row_ok) continue;
-    const int c0 = j * kBN + wg * 32;
+    const int c0 = (t.n_ct - 1 - j) * kBN + wg * 32;
     const bool full = (c0 + 31 <= lim) && (bits == nullptr);
     uint64_t acc2 = 0;
 #pragma unroll
@@ -447,9 +447,10 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs0,
         if (j >= L::NS && !mbar_wait(&misc->k_empty[s], ((j / L::NS) - 1) & 1, abort, err)) break;
         uint8_t* st = smem + L::OFF_K + s * L::STAGE;
         mbar_arrive_expect_tx(&misc->k_full[s], kBN * DS * 2 + (kTeacher ? kBN * DT * 2 : 0));
-        issue_tile_loads(st, &tm_ks, &misc->k_full[s], DS, j * kBN, t.hs, t.b);
+        issue_tile_loads(st, &tm_ks, &misc->k_full[s], DS, (t.n_ct - 1 - j) * kBN, t.hs, t.b);
         if (kTeacher)
-          issue_tile_loads(st + kBN * DS * 2, &tm_kt, &misc->k_full[s], DT, j * kBN, t.ht, t.b);
+          issue_tile_loads(st + kBN * DS * 2, &tm_kt, &misc->k_full[s], DT, (t.n_ct - 1 - j) * kBN,
+                           t.ht, t.b);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -514,7 +515,7 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs0,
         __syncwarp();
         if (lane == 0) mbar_arrive(&misc->s_empty[bf]);
         if (!row_valid) continue;
-        const int c0 = j * kBN + wg * 32;
+        const int c0 = (t.n_ct - 1 - j) * kBN + wg * 32;
         const bool full = (c0 + 31 <= lim) && (bits == nullptr);
         if (!full) {
           // masked columns get a large finite negative score: e^(s - m) = 0 and
@@ -540,11 +541,15 @@ sm100_forward_kernel(const __grid_constant__ CUtensorMap tm_qs0,
         if (my < -1.0e29f) continue;  // no valid column in this chunk
         const float ms_new = fmaxf(m_s, mx * cs);
         const float mt_new = fmaxf(m_t, my * ct);
-        l_s *= ex2(m_s - ms_new);
-        const float beta = ex2(m_t - mt_new);
-        l_t *= beta;
-        ay *= beta;
-        ax *= beta;
+        // key tiles run from the diagonal down, so the row maxima are mostly
+        // found in the first tile and later tiles skip the rescale
+        if (__any_sync(__activemask(), ms_new > m_s || mt_new > m_t)) {
+          l_s *= ex2(m_s - ms_new);
+          const float beta = ex2(m_t - mt_new);
+          l_t *= beta;
+          ay *= beta;
+          ax *= beta;
+        }
         // packed pairs: l_s += e^(ss - m_s); l_t += e^(st - m_t);
         // ay += e^(st - m_t) * st_raw; ax += e^(st - m_t) * ss_raw
         const uint64_t cs2 = f2pack(cs, cs), ct2 = f2pack(ct, ct);
