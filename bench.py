@@ -30,8 +30,6 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-E2E_SLICE = 8      # heads per host->device slice in the end-to-end measurement
-E2E_FIRST = 2      # heads of the first slice (the one copy not hidden under compute)
 METRIC = "KL fwd+bwd tokens/s, LLaMA3-8B heads @32K ctx; % bf16 tensor peak"
 WORKLOAD = "llama3_8b_32k"
 
@@ -440,11 +438,14 @@ def main():
     # ---- end to end from pinned host buffers through the public API
     e2e = None
     if not args.no_e2e:
-        # The inputs of each relation arrive from pinned host memory in slices of
-        # E2E_SLICE heads, each its own leaf tensor and its own attn_kl_align call
-        # (the loss is a sum over heads).  All copies go out on a copy stream at
-        # the start of the step; the forward of slice k waits only for slice k's
-        # copy, so the PCIe transfer of later slices runs under earlier compute.
+        # Each step's inputs come from pinned host memory through the public
+        # API, as a training loop with a prefetching loader runs it: two sets
+        # of device input buffers; while step k computes on set k % 2, a copy
+        # stream fills set (k + 1) % 2 with step k + 1's inputs (after step
+        # k - 1, the last user of that set, is done).  Every step carries one
+        # full host->device copy of its inputs and one device->host read of its
+        # loss (into pinned memory; the host reads step k - 1's loss during
+        # step k, so the GPU never waits for the host).
         numa = None if args.no_numa else gpu_local_cpus(dev)
         saved_affinity = None
         if numa:
@@ -453,37 +454,39 @@ def main():
             # engines of N GPUs do not all read across the socket link
             saved_affinity = os.sched_getaffinity(0)
             os.sched_setaffinity(0, numa)
-        slices = []
-        for ri, r in enumerate(cfg.relations):
-            H = students[r].shape[1]
-            # slice boundaries: E2E_SLICE heads each, except that the first
-            # slice of the step is E2E_FIRST heads (its copy is the one that
-            # nothing hides)
-            bounds = list(range(0, H, E2E_SLICE)) + [H]
-            if ri == 0 and E2E_FIRST < min(H, E2E_SLICE):
-                bounds = [0, E2E_FIRST] + bounds[1:]
-            for h0, h1 in zip(bounds[:-1], bounds[1:]):
-                hs = students[r].detach()[:, h0:h1].contiguous().cpu().pin_memory()
-                ht = teachers[r][:, h0:h1].contiguous().cpu().pin_memory()
-                slices.append((hs, ht, torch.empty_like(hs, device=dev),
-                               torch.empty_like(ht, device=dev)))
+        host = [(students[r].detach().cpu().pin_memory(), teachers[r].cpu().pin_memory())
+                for r in cfg.relations]
+        loss_host = torch.zeros(2, dtype=torch.float32).pin_memory()
         if saved_affinity is not None:
             os.sched_setaffinity(0, saved_affinity)
-        h2d = sum(x.numel() * x.element_size() for sl in slices for x in sl[:2])
+        bufs = [[(torch.empty_like(hs, device=dev), torch.empty_like(ht, device=dev))
+                 for hs, ht in host] for _ in range(2)]
+        h2d = sum(x.numel() * x.element_size() for pair in host for x in pair)
         copy_stream = torch.cuda.Stream(device=dev)
-        copied = [torch.cuda.Event() for _ in slices]
+        copied = [torch.cuda.Event() for _ in range(2)]
+        done = [torch.cuda.Event() for _ in range(2)]
+        loss_ready = [torch.cuda.Event() for _ in range(2)]
+        state = {"k": 0, "last": None}
 
-        def e2e_step():
-            cur = torch.cuda.current_stream(dev)
-            copy_stream.wait_stream(cur)   # the previous step is done with the buffers
+        def prefetch(k):
+            """Copies of step k's inputs into buffer set k % 2 (copy stream)."""
             with torch.cuda.stream(copy_stream):
-                for (hs, ht, ds, dt), ev in zip(slices, copied):
+                if k >= 2:
+                    copy_stream.wait_event(done[k % 2])   # step k - 2 is done with the set
+                for (hs, ht), (ds, dt) in zip(host, bufs[k % 2]):
                     ds.copy_(hs, non_blocking=True)
                     dt.copy_(ht, non_blocking=True)
-                    ev.record(copy_stream)
+                copied[k % 2].record(copy_stream)
+
+        def e2e_step():
+            k = state["k"]
+            cur = torch.cuda.current_stream(dev)
+            if k == 0:
+                prefetch(0)
+            prefetch(k + 1)                  # runs under this step's compute
+            cur.wait_event(copied[k % 2])
             total = None
-            for (_, _, ds, dt), ev in zip(slices, copied):
-                cur.wait_event(ev)
+            for ds, dt in bufs[k % 2]:
                 s_leaf = ds.detach().requires_grad_(True)
                 l = attn_kl_align(s_leaf, s_leaf, dt, dt, None, cfg.causal)
                 total = l if total is None else total + l
@@ -492,7 +495,13 @@ def main():
                 red = total.detach().clone()
                 dist.all_reduce(red)
                 total = red
-            return float(total.item())   # device -> host read of the loss
+            loss_host[k % 2].copy_(total.detach(), non_blocking=True)   # device -> host
+            loss_ready[k % 2].record(cur)
+            done[k % 2].record(cur)
+            if k > 0:                        # the host reads the previous step's loss
+                loss_ready[(k - 1) % 2].synchronize()
+                state["last"] = float(loss_host[(k - 1) % 2])
+            state["k"] = k + 1
 
         for _ in range(max(1, args.warmup)):
             e2e_step()
@@ -501,6 +510,7 @@ def main():
         k0.record()
         for _ in range(args.steps):
             e2e_step()
+        torch.cuda.current_stream(dev).wait_stream(copy_stream)   # the last prefetch too
         k1.record()
         barrier()
         e_ms = torch.tensor([k0.elapsed_time(k1)], device=dev)
@@ -513,7 +523,7 @@ def main():
         c0.record(copy_stream)
         with torch.cuda.stream(copy_stream):
             for _ in range(args.steps):
-                for hs, ht, ds, dt in slices:
+                for (hs, ht), (ds, dt) in zip(host, bufs[0]):
                     ds.copy_(hs, non_blocking=True)
                     dt.copy_(ht, non_blocking=True)
         c1.record(copy_stream)
@@ -530,7 +540,9 @@ def main():
                "h2d_gbs_per_rank_copy_only": h2d / (copy_ms / 1e3) / 1e9,
                "exposed_ms_per_step": e_step - ms_step,
                "bound": "host->device copies" if copy_ms >= ms_step else "device compute",
-               "staging_numa_local": bool(numa)}
+               "staging_numa_local": bool(numa),
+               "input_pipeline": "two device input sets: step k+1's copies run under step k; "
+                                 "loss read one step behind into pinned memory"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
